@@ -1,0 +1,119 @@
+// llmx::Tensor -- the tensor type llmx's attention op takes.
+//
+// Same public surface as the reference (include/llmx/tensor.h:17-177):
+// ScalarType, DeviceType, Device, DataPtr, Tensor with dims/strides/capacity,
+// allocate / resize / to_device, and the llmx_allocate / llmx_free /
+// llmx_copy helpers.  Differences, all internal:
+//  * CUDA tensors live in device memory (cudaMalloc + zero fill) instead of
+//    managed memory (tensor.cpp:64-70);
+//  * ownership is a shared control block, so copies share storage and the
+//    last owner frees it (the reference keeps a refcount map, tensor.cpp:155-160);
+//  * a Tensor built on an external pointer never owns it (tensor.cpp:218-224).
+#pragma once
+
+#include <cstddef>
+#include <functional>
+#include <memory>
+#include <numeric>
+#include <optional>
+#include <vector>
+
+namespace llmx {
+
+enum class ScalarType { kFP32, kFP16, kBF16 };
+
+size_t get_scalar_size(ScalarType dtype);
+
+enum class DeviceType { kCPU, kCUDA };
+
+struct Device {
+  DeviceType type = DeviceType::kCPU;
+  int id = -1;
+
+  Device() = default;
+  Device(DeviceType type, int id = -1) : type(type), id(id) {}
+
+  bool operator==(const Device &other) const { return type == other.type && id == other.id; }
+  bool operator!=(const Device &other) const { return !(*this == other); }
+};
+
+void *llmx_allocate(size_t nbytes, Device device);
+void llmx_free(void *data, Device device);
+void llmx_copy(Device src_device, Device dst_device, const void *src, void *dst, size_t nbytes);
+
+// Pointer plus (for storage the allocator made) a shared owner.
+class DataPtr {
+ public:
+  DataPtr() = default;
+  explicit DataPtr(void *ptr) : ptr_(ptr) {}  // non-owning
+  DataPtr(void *ptr, Device device);          // owning: frees with llmx_free
+
+  void *ptr() const noexcept { return ptr_; }
+  template <typename T>
+  T *ptr() const noexcept {
+    return reinterpret_cast<T *>(ptr_);
+  }
+  bool owns() const noexcept { return owner_ != nullptr; }
+  long use_count() const noexcept { return owner_ ? owner_.use_count() : 0; }
+  bool operator==(std::nullptr_t) const noexcept { return ptr_ == nullptr; }
+  bool operator!=(std::nullptr_t) const noexcept { return ptr_ != nullptr; }
+
+ private:
+  void *ptr_ = nullptr;
+  std::shared_ptr<void> owner_;
+};
+
+class Tensor {
+ public:
+  Tensor() = default;
+  Tensor(const std::vector<int> &dims, ScalarType dtype, Device device);  // allocates, zeroed
+  Tensor(void *data, const std::vector<int> &dims, ScalarType dtype, Device device);  // wraps
+
+  ScalarType dtype() const noexcept { return dtype_; }
+  void dtype(ScalarType dtype) noexcept { dtype_ = dtype; }
+  std::vector<int> dims() const noexcept { return dims_; }
+  int dim(int axis) const noexcept { return dims_[axis]; }
+  int stride(int axis) const noexcept { return strides_[axis]; }
+  int ndim() const noexcept { return static_cast<int>(dims_.size()); }
+  Device device() const noexcept { return device_; }
+  const DataPtr &data() const noexcept { return data_; }
+  DataPtr &data() noexcept { return data_; }
+  const void *const_data_ptr() const noexcept { return data_.ptr(); }
+  void *data_ptr() noexcept { return data_.ptr(); }
+  template <typename T>
+  const T *const_data_ptr() const noexcept {
+    return data_.template ptr<T>();
+  }
+  template <typename T>
+  T *data_ptr() noexcept {
+    return data_.template ptr<T>();
+  }
+
+  bool is_valid() const noexcept { return data_.ptr() != nullptr && capacity_ > 0; }
+  bool contiguous() const noexcept;
+  size_t nbytes() const noexcept { return capacity_ * get_scalar_size(dtype_); }
+  size_t capacity() const noexcept { return capacity_; }
+  size_t count(int axis = 0) const noexcept { return size_t(dims_[axis]) * strides_[axis]; }
+  size_t numel() const noexcept {
+    return std::accumulate(dims_.begin(), dims_.end(), size_t(1), std::multiplies<>{});
+  }
+
+  // Makes room for numel() elements (reallocating, zeroed, only when growing).
+  void allocate();
+  // Metadata-only reshape; storage is kept (tensor_test.cpp:62-100).
+  void resize(const std::vector<int> &dims);
+  // Moves storage to `device`, copying the contents when `transfer`.
+  void to_device(Device device, bool transfer = true);
+
+ private:
+  void set_dims(const std::vector<int> &dims);
+
+  DataPtr data_;
+  ScalarType dtype_ = ScalarType::kFP32;
+  std::vector<int> dims_;
+  std::vector<int> strides_;
+  size_t capacity_ = 0;
+  Device device_ = Device(DeviceType::kCPU);
+};
+
+}  // namespace llmx

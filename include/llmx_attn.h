@@ -1,0 +1,147 @@
+/*
+ * llmx_attn.h -- C ABI of the B200 (sm_100a) attention forward engine.
+ *
+ * Plain pointers and sizes only; every entry point returns an llmx_status and
+ * allocates nothing.  All device pointers must live on the CUDA device that is
+ * current on the calling thread; work is enqueued on the caller's stream.
+ *
+ * Reference interfaces this ABI replaces (paths inside DucHUNG312/llmx):
+ *   llmx_single_mha_attention   include/llmx/cuda/attention/attention_api.h:8-14
+ *                               src/cuda/attention/attention_api.cpp:14-72
+ *   MHAParams (+ normalize)     include/llmx/cuda/attention/params.h:7-51
+ *   single_mha_attention_launcher
+ *                               include/llmx/cuda/attention/device/single_mha_kernel.cuh:595-635
+ * The reference signature is one causal sequence on stream 0; llmx_attn_fwd
+ * adds the batch axis, a non-causal mode, per-sequence lengths (padding),
+ * fp32, a caller stream, an optional log-sum-exp output and a caller-owned
+ * workspace for split-KV decoding.
+ */
+#ifndef LLMX_ATTN_H
+#define LLMX_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LLMX_ATTN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define LLMX_API __attribute__((visibility("default")))
+#else
+#define LLMX_API
+#endif
+
+typedef enum llmx_status {
+  LLMX_OK = 0,
+  LLMX_ERR_INVALID_ARGUMENT = 1, /* bad shape, stride, pointer or value      */
+  LLMX_ERR_UNSUPPORTED = 2,      /* valid request no kernel here implements  */
+  LLMX_ERR_WORKSPACE_TOO_SMALL = 3,
+  LLMX_ERR_CUDA = 4,             /* a CUDA runtime call or launch failed     */
+  LLMX_ERR_TIMEOUT = 5,          /* a bounded device-side wait expired       */
+  LLMX_ERR_NO_DEVICE = 6
+} llmx_status;
+
+/* Element types, numbered as llmx::ScalarType (include/llmx/tensor.h:19). */
+typedef enum llmx_dtype { LLMX_FP32 = 0, LLMX_FP16 = 1, LLMX_BF16 = 2 } llmx_dtype;
+
+/* Kernel selection.  AUTO picks per request; the others force one family and
+ * fail with LLMX_ERR_UNSUPPORTED when it cannot run the request. */
+typedef enum llmx_attn_algo {
+  LLMX_ALGO_AUTO = 0,
+  LLMX_ALGO_SIMT = 1,    /* fp32-accumulating CUDA-core kernel, every shape  */
+  LLMX_ALGO_DECODE = 2,  /* split-KV decode, max_q_len == 1, fp16/bf16       */
+  LLMX_ALGO_TCGEN05 = 3  /* TMA + tcgen05/TMEM prefill, fp16/bf16, D 64/128 */
+} llmx_attn_algo;
+
+/*
+ * One attention forward over a padded batch.
+ *   q, o : [batch, max_q_len,  n_heads,    head_dim]
+ *   k, v : [batch, max_kv_len, n_kv_heads, head_dim]
+ * given by element strides {batch, seq, head}; the head_dim stride is 1.
+ * Sequence b uses its first q_lens[b] query rows and kv_lens[b] keys (NULL
+ * means the max extent; device int32 arrays, values are clamped to
+ * [0, max]).  Query row i of sequence b attends to key j when
+ *   j < kv_len_b,
+ *   causal:  j <= i + (kv_len_b - q_len_b)        (bottom-right, mask.h:54-63)
+ *   window:  (i + kv_len_b - q_len_b) - j <= sliding_window  (mask.h:60,66)
+ * Score = q.k * sm_scale, then tanh(s/cap)*cap if logits_soft_cap > 0
+ * (params.h:35-50), then + alibi_slopes[h] * j (mask.h:75-77).
+ * Query rows past q_len_b and rows that see no key are written as 0 (their
+ * lse as -inf).  GQA: head h reads kv head h / (n_heads / n_kv_heads).
+ */
+typedef struct llmx_attn_params {
+  int32_t dtype;      /* llmx_dtype of q, k, v and o                    */
+  int32_t batch;      /* >= 1                                            */
+  int32_t n_heads;    /* >= 1                                            */
+  int32_t n_kv_heads; /* >= 1, divides n_heads                           */
+  int32_t head_dim;   /* 1..256                                          */
+  int32_t max_q_len;  /* >= 1                                            */
+  int32_t max_kv_len; /* >= 1                                            */
+  int32_t algo;       /* llmx_attn_algo                                  */
+  const void *q;
+  const void *k;
+  const void *v;
+  void *o;
+  int64_t q_stride[3]; /* elements: batch, seq, head                     */
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  const int32_t *q_lens;      /* device [batch] or NULL                  */
+  const int32_t *kv_lens;     /* device [batch] or NULL                  */
+  const float *alibi_slopes;  /* device [n_heads] fp32 or NULL           */
+  float sm_scale;
+  int32_t causal;             /* 1 = causal (the reference's only mode)  */
+  int32_t sliding_window;     /* < 0 disables                            */
+  float logits_soft_cap;      /* <= 0 disables                           */
+  float *lse;                 /* NULL or device [batch, n_heads, max_q_len] fp32 */
+  void *workspace;            /* device scratch for split-KV partials    */
+  size_t workspace_bytes;
+} llmx_attn_params;
+
+/* Fills *p with defaults: contiguous-stride fields zero, causal = 1,
+ * sliding_window = -1, logits_soft_cap = 0, algo = AUTO. */
+LLMX_API llmx_status llmx_attn_params_init(llmx_attn_params *p);
+
+/* Sets the four stride triples for contiguous [B, S, H, D] tensors. */
+LLMX_API llmx_status llmx_attn_set_contiguous_strides(llmx_attn_params *p);
+
+/* Workspace bytes llmx_attn_fwd wants for *p (0 when none).  A call given
+ * less (or NULL) still runs, without splitting the KV axis. */
+LLMX_API llmx_status llmx_attn_workspace_size(const llmx_attn_params *p, size_t *bytes);
+
+/* Enqueues the forward on `stream` (a cudaStream_t; NULL = legacy stream).
+ * Replaces llmx_single_mha_attention (attention_api.cpp:14-72) for batched,
+ * padded and non-causal requests. */
+LLMX_API llmx_status llmx_attn_fwd(const llmx_attn_params *p, void *stream);
+
+/* The reference's entry point with plain pointers: one causal sequence,
+ * q/o [q_len, n_heads, head_dim], k/v [kv_len, n_kv_heads, head_dim],
+ * contiguous.  Same arguments and meaning as
+ * llmx::llmx_single_mha_attention (attention_api.h:8-14) plus dtype, the
+ * sizes the Tensor carried, and a stream. */
+LLMX_API llmx_status llmx_single_mha_attention_c(void *output, const void *q, const void *k, const void *v,
+                                        const float *alibi_slopes, int32_t dtype, int32_t q_len,
+                                        int32_t kv_len, int32_t n_heads, int32_t n_kv_heads,
+                                        int32_t head_dim, float sm_scale, int32_t sliding_window,
+                                        float logits_soft_cap, void *stream);
+
+/* Which kernel family llmx_attn_fwd would run for *p (an llmx_attn_algo). */
+LLMX_API llmx_status llmx_attn_select_algo(const llmx_attn_params *p, int32_t *algo);
+
+/* Synchronises `device` and reads (and optionally clears) its device-side
+ * error word: LLMX_ERR_TIMEOUT if any kernel gave up on a bounded wait. */
+LLMX_API llmx_status llmx_attn_device_status(int32_t device, int32_t clear);
+
+LLMX_API const char *llmx_status_string(llmx_status s);
+/* Message of the last failing call on this thread ("" if none). */
+LLMX_API const char *llmx_attn_last_error(void);
+LLMX_API int32_t llmx_attn_abi_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* LLMX_ATTN_H */

@@ -1,0 +1,120 @@
+// llmx::Tensor storage and copies (host code).  Semantics of the reference's
+// src/tensor.cpp:1-263 that callers observe are kept: allocation zero-fills,
+// resize is metadata-only, allocate() reallocates only when growing, and
+// to_device moves (optionally copies) storage between host and a CUDA device.
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "llmx/tensor.h"
+
+namespace llmx {
+namespace {
+void cuda_ok(cudaError_t e, const char *what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+}  // namespace
+
+size_t get_scalar_size(ScalarType dtype) {
+  switch (dtype) {
+    case ScalarType::kFP32: return 4;
+    case ScalarType::kFP16: return 2;
+    case ScalarType::kBF16: return 2;
+  }
+  throw std::invalid_argument("unsupported scalar type");
+}
+
+void *llmx_allocate(size_t nbytes, Device device) {
+  if (nbytes == 0) return nullptr;
+  if (device.type == DeviceType::kCPU) {
+    void *p = nullptr;
+    if (posix_memalign(&p, 64, nbytes) != 0) throw std::bad_alloc();
+    std::memset(p, 0, nbytes);
+    return p;
+  }
+  int prev = 0;
+  cuda_ok(cudaGetDevice(&prev), "cudaGetDevice");
+  cuda_ok(cudaSetDevice(device.id < 0 ? 0 : device.id), "cudaSetDevice");
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, nbytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, nbytes);
+  cudaSetDevice(prev);
+  cuda_ok(e, "cudaMalloc");
+  return p;
+}
+
+void llmx_free(void *data, Device device) {
+  if (data == nullptr) return;
+  if (device.type == DeviceType::kCPU) {
+    std::free(data);
+  } else {
+    cudaFree(data);
+  }
+}
+
+void llmx_copy(Device src_device, Device dst_device, const void *src, void *dst,
+                        size_t nbytes) {
+  if (nbytes == 0) return;
+  if (src == nullptr || dst == nullptr) throw std::invalid_argument("llmx_copy: null pointer");
+  if (src_device.type == DeviceType::kCPU && dst_device.type == DeviceType::kCPU) {
+    std::memcpy(dst, src, nbytes);
+    return;
+  }
+  cuda_ok(cudaMemcpy(dst, src, nbytes, cudaMemcpyDefault), "cudaMemcpy");
+}
+
+DataPtr::DataPtr(void *ptr, Device device)
+    : ptr_(ptr), owner_(ptr, [device](void *p) { llmx_free(p, device); }) {}
+
+Tensor::Tensor(const std::vector<int> &dims, ScalarType dtype, Device device)
+    : dtype_(dtype), device_(device) {
+  set_dims(dims);
+  allocate();
+}
+
+Tensor::Tensor(void *data, const std::vector<int> &dims, ScalarType dtype, Device device)
+    : data_(data), dtype_(dtype), device_(device) {
+  set_dims(dims);
+  capacity_ = numel();
+}
+
+void Tensor::set_dims(const std::vector<int> &dims) {
+  dims_ = dims;
+  strides_.assign(dims.size(), 1);
+  for (int i = static_cast<int>(dims.size()) - 2; i >= 0; --i) strides_[i] = strides_[i + 1] * dims[i + 1];
+}
+
+bool Tensor::contiguous() const noexcept {
+  if (strides_.empty()) return true;
+  if (strides_.back() != 1) return false;
+  for (int i = static_cast<int>(dims_.size()) - 2; i >= 0; --i)
+    if (strides_[i] != strides_[i + 1] * dims_[i + 1]) return false;
+  return true;
+}
+
+void Tensor::allocate() {
+  const size_t n = numel();
+  if (data_.ptr() != nullptr && n <= capacity_) return;
+  void *p = llmx_allocate(n * get_scalar_size(dtype_), device_);
+  data_ = DataPtr(p, device_);
+  capacity_ = n;
+}
+
+void Tensor::resize(const std::vector<int> &dims) { set_dims(dims); }
+
+void Tensor::to_device(Device device, bool transfer) {
+  if (device == device_) return;
+  if (!is_valid()) {
+    device_ = device;
+    return;
+  }
+  void *p = llmx_allocate(capacity_ * get_scalar_size(dtype_), device);
+  if (transfer) llmx_copy(device_, device, data_.ptr(), p, capacity_ * get_scalar_size(dtype_));
+  data_ = DataPtr(p, device);
+  device_ = device;
+}
+
+}  // namespace llmx
