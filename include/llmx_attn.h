@@ -128,6 +128,27 @@ LLMX_API llmx_status llmx_single_mha_attention_c(void *output, const void *q, co
                                         int32_t head_dim, float sm_scale, int32_t sliding_window,
                                         float logits_soft_cap, void *stream);
 
+/* Split-KV decode that allocates nothing, for callers that cannot allocate
+ * device memory after start-up (a fixed memory budget reserved up front, or a
+ * latency-critical loop that must not hit cudaMalloc's implicit device-wide
+ * synchronisation) and so cannot pass a workspace.  No counterpart in the
+ * reference.  Same request and results as llmx_attn_fwd on the decode path
+ * (fp16/bf16, max_q_len == 1, head_dim 64/128/256); the split partials live
+ * in one static device array of LLMX_DECODE_NOALLOC_SCRATCH_BYTES per GPU,
+ * held by every GPU that loads the library until the process exits.
+ *  - Requests needing more scratch than that are refused with
+ *    LLMX_ERR_WORKSPACE_TOO_SMALL (need = n_splits * batch * n_heads *
+ *    (head_dim + 1) * 4 bytes; 256-key splits).
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress, once per device, with that device current); make
+ *    that first call before any stream capture.
+ *  - All calls on a device share the array: calls that overlap on the GPU
+ *    (different streams, or concurrent host threads) race and corrupt each
+ *    other's results.  p->workspace is ignored.
+ *  - Calls no cudaMalloc, cudaFree or other allocating routine. */
+#define LLMX_DECODE_NOALLOC_SCRATCH_BYTES (32u << 20)
+LLMX_API llmx_status llmx_attn_decode_noalloc(const llmx_attn_params *p, void *stream);
+
 /* Which kernel family llmx_attn_fwd would run for *p (an llmx_attn_algo). */
 LLMX_API llmx_status llmx_attn_select_algo(const llmx_attn_params *p, int32_t *algo);
 

@@ -180,6 +180,25 @@ llmx_status current_device(int *dev, const DeviceInfo **info) {
 }
 
 }  // namespace
+
+llmx_status prepare_decode_request(const llmx_attn_params *p, AttnArgs *a) {
+  llmx_status s = validate(p, a);
+  if (s != LLMX_OK) return s;
+  if (!decode_supports(*a))
+    return fail(LLMX_ERR_UNSUPPORTED,
+                "decode kernel needs fp16/bf16, max_q_len == 1, head_dim 64/128/256 and 16-byte "
+                "aligned rows");
+  int dev = 0;
+  const DeviceInfo *info = nullptr;
+  s = current_device(&dev, &info);
+  if (s != LLMX_OK) return s;
+  a->err = info->err;
+  a->num_sms = info->num_sms;
+  return LLMX_OK;
+}
+
+llmx_status record_error(llmx_status s, const char *msg) { return fail(s, msg); }
+
 }  // namespace llmx_b200
 
 using namespace llmx_b200;

@@ -18,6 +18,9 @@
 // warps are merged.  With one split the CTA writes O directly; otherwise it
 // writes a normalised partial (O_s, lse_s) and the combine kernel computes
 //   lse = log sum_s exp(lse_s),  O = sum_s exp(lse_s - lse) O_s.
+#include <cstdio>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace llmx_b200 {
@@ -334,3 +337,74 @@ cudaError_t launch_decode(const AttnArgs &a, const DecodePlan &p, void *ws, cuda
 }
 
 }  // namespace llmx_b200
+
+// ---------------------------------------------------------------------------
+// Split-KV decode that allocates nothing.
+//
+// Some callers cannot call cudaMalloc or hand us a workspace: serving engines
+// that fix their whole device-memory budget at start-up (KV cache, weights and
+// activations reserved up front, any later allocation treated as a failure),
+// and latency-critical loops that must not trigger cudaMalloc's implicit
+// device-wide synchronisation.  For them the split partials live in a
+// statically sized device array that this file owns.  Every GPU that loads
+// the library holds the array until the process exits.
+// ---------------------------------------------------------------------------
+namespace llmx_b200 {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(LLMX_DECODE_NOALLOC_SCRATCH_BYTES);
+
+// Host code must never use this name as a device address: on the host it is
+// a stand-in object, so its address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+constexpr int kMaxNoAllocDevices = 64;
+float *g_noalloc_ptr[kMaxNoAllocDevices];
+cudaError_t g_noalloc_status[kMaxNoAllocDevices];
+std::once_flag g_noalloc_once[kMaxNoAllocDevices];
+
+// Device address of the scratch array on `dev` (which must be current).
+// Looked up once per device; cudaGetSymbolAddress allocates nothing.
+cudaError_t noalloc_scratch(int dev, float **out) {
+  std::call_once(g_noalloc_once[dev], [dev] {
+    void *p = nullptr;
+    g_noalloc_status[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    g_noalloc_ptr[dev] = g_noalloc_status[dev] == cudaSuccess ? static_cast<float *>(p) : nullptr;
+  });
+  *out = g_noalloc_ptr[dev];
+  if (g_noalloc_status[dev] == cudaSuccess && *out == nullptr) return cudaErrorInvalidSymbol;
+  return g_noalloc_status[dev];
+}
+
+}  // namespace
+}  // namespace llmx_b200
+
+extern "C" llmx_status llmx_attn_decode_noalloc(const llmx_attn_params *p, void *stream) {
+  using namespace llmx_b200;
+  AttnArgs a;
+  llmx_status s = prepare_decode_request(p, &a);
+  if (s != LLMX_OK) return s;
+  // Same split plan as llmx_attn_fwd with an unlimited workspace, so results
+  // match it; requests whose partials exceed the array are refused.
+  const DecodePlan plan = plan_decode(a, SIZE_MAX, true);
+  if (plan.ws_bytes > kNoAllocScratchBytes) {
+    char msg[200];
+    snprintf(msg, sizeof msg,
+             "llmx_attn_decode_noalloc: request needs %zu bytes of split-KV scratch; the static array "
+             "holds %zu (LLMX_DECODE_NOALLOC_SCRATCH_BYTES)",
+             plan.ws_bytes, kNoAllocScratchBytes);
+    return record_error(LLMX_ERR_WORKSPACE_TOO_SMALL, msg);
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxNoAllocDevices)
+    return record_error(LLMX_ERR_NO_DEVICE, "llmx_attn_decode_noalloc: no usable current device");
+  float *scratch = nullptr;
+  cudaError_t e = noalloc_scratch(dev, &scratch);
+  if (e != cudaSuccess)
+    return record_error(LLMX_ERR_CUDA, "llmx_attn_decode_noalloc: cudaGetSymbolAddress failed");
+  // Every partial the combine reads is written first by its split, so the
+  // array's previous contents never need clearing.
+  e = launch_decode(a, plan, scratch, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return record_error(LLMX_ERR_CUDA, cudaGetErrorString(e));
+  return LLMX_OK;
+}

@@ -7,6 +7,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "llmx_attn.h"
+
 namespace llmx_b200 {
 
 // Device-side error codes OR-ed into the per-device error word.
@@ -42,6 +44,12 @@ struct DecodePlan {
 };
 
 DecodePlan plan_decode(const AttnArgs &a, size_t ws_available, bool have_ws);
+
+// Validation shared with entry points outside attn_api.cu: checks *p, that
+// the split-KV decode family can run it, and the current device; fills *a
+// (error word and SM count included).  Records the message on failure.
+llmx_status prepare_decode_request(const llmx_attn_params *p, AttnArgs *a);
+llmx_status record_error(llmx_status s, const char *msg);
 
 cudaError_t launch_simt(const AttnArgs &a, cudaStream_t s);
 cudaError_t launch_decode(const AttnArgs &a, const DecodePlan &plan, void *ws, cudaStream_t s);
