@@ -1,7 +1,571 @@
-// Placeholder until the tcgen05 prefill kernel lands.
-#include "attn_internal.h"
+// Fused attention forward on Blackwell tensor cores (sm_100a): TMA-staged
+// Q/K/V tiles, S = QK^T and O += PV on tcgen05.mma with both accumulators in
+// tensor memory, and scale + soft-cap + ALiBi + causal / window / length
+// masks + online softmax fused between the two GEMMs.  Scores never leave
+// the SM.
+//
+// Reference path replaced: SingleMHACollectiveMainloop + SingleMHAKernel
+// (include/llmx/cuda/attention/device/single_mha_kernel.cuh:30-345,479-593),
+// an SM80 mma.sync kernel with a 64x64 tile, one cp.async stage and
+// register-resident accumulators.  Semantics kept: bottom-right causal
+// alignment and window (mask.h:41-81), ALiBi as + slope*j (mask.h:75-77),
+// soft-cap tanh(s*scale/cap)*cap (params.h:35-50), P rounded to the input
+// type before PV (single_mha_kernel.cuh:232-233), GQA head h -> kv head
+// h / group.
+//
+// CTA = 2 query tiles of 128 rows of one (batch, head); 10 warps:
+//   warps 0-3  softmax for query tile 0 (thread r owns row r = TMEM lane r)
+//   warps 4-7  softmax for query tile 1
+//   warp  8    tensor-memory allocation + MMA issue (one thread)
+//   warp  9    TMA producer (one thread)
+// Tensor memory (512 columns x 128 lanes of 32 bit):
+//   [0,128) S0 / P0, [128,256) S1 / P1, [256,256+D) O0, [256+D,256+2D) O1.
+// P (16-bit, two per column) overwrites the first 64 columns of its S.
+//
+// Per KV block j of 128 keys the MMA thread issues, in order,
+//   O0 += P0(j) V(j),   S0(j+1) = Q0 K(j+1)^T,   O1 += P1(j) V(j),   S1(j+1)
+// so each softmax warpgroup's exponentials overlap the other tile's GEMMs;
+// tcgen05 operations from one thread execute in issue order, which is what
+// lets S0(j+1) overwrite P0(j) right after PV0(j) is issued.
+//
+// Online softmax: running max m and sum l per row in log2 units.  The max is
+// only moved (and O rescaled in tensor memory) when a block raises it by more
+// than 8 (a factor 256), so P <= 256 and O rescales are rare; the final
+// O / l is the same softmax.
+//
+// Every mbarrier wait is bounded (1 s); on expiry the kernel records
+// kDevErrTimeout in the device error word, unwinds all roles, waits (bounded)
+// for its in-flight TMA loads and MMAs, frees tensor memory and exits.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace llmx_b200 {
-bool sm100_supports(const AttnArgs &) { return false; }
-cudaError_t launch_sm100(const AttnArgs &, cudaStream_t) { return cudaErrorNotSupported; }
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;       // query rows per tile
+constexpr int kTiles = 2;      // query tiles per CTA
+constexpr int kBN = 128;       // keys per KV block
+constexpr int kThreads = 320;  // 8 softmax warps + MMA warp + TMA warp
+constexpr int kMmaWarp = 8;
+constexpr int kTmaWarp = 9;
+constexpr uint64_t kTimeoutNs = 1000000000ull;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;
+
+template <int D>
+struct Cfg {
+  static constexpr int kChunks = D / 64;          // 128-byte wide column chunks of a tile
+  static constexpr int kChunkBytes = 128 * 128;   // 128 rows x 128 bytes
+  static constexpr int kTileBytes = 128 * D * 2;  // one 128-row tile of 16-bit elements
+  static constexpr int kStages = D == 128 ? 2 : 3;
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = kQOff + kTiles * kTileBytes;
+  static constexpr int kVOff = kKOff + kStages * kTileBytes;
+  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
+  static constexpr int kSmemBytes = kBarOff + 1024 + 1024;  // barriers + alignment slack
+  static constexpr uint32_t kTmemS0 = 0, kTmemS1 = 128;
+  static constexpr uint32_t kTmemO0 = 256, kTmemO1 = 256 + D;
+  static constexpr uint32_t kTmemCols = 512;
+};
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
+  uint64_t s_full[2], p_full[2], o_done[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  volatile int abort_flag;
+};
+
+__device__ __forceinline__ void set_abort(Bars *bars, unsigned int *err) {
+  bars->abort_flag = 1;
+  raise_error(err, kDevErrTimeout);
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (std::is_same<T, __half>::value) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+  } else {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+  }
+}
+
+// Key-block range of the CTA: blocks [n_start, n_start + nb*kBN).
+struct BlockRange {
+  int n_start, nb;
+};
+
+__device__ __forceinline__ BlockRange block_range(const AttnArgs &a, int m0, int ql, int kl) {
+  BlockRange r{0, 0};
+  if (m0 >= ql || kl <= 0) return r;
+  const int off = kl - ql;
+  const int r_last = min(m0 + kTiles * kBM, ql) - 1;
+  const int hi = a.causal ? min(kl, r_last + off + 1) : kl;
+  int lo = a.window >= 0 ? max(0, m0 + off - a.window) : 0;
+  lo = (lo / kBN) * kBN;
+  if (hi > lo) {
+    r.n_start = lo;
+    r.nb = (hi - lo + kBN - 1) / kBN;
+  }
+  return r;
+}
+
+// ---------------------------------------------------------------- TMA role
+template <int D>
+__device__ void tma_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k, const CUtensorMap *tm_v,
+                         uint8_t *smem, Bars *bars, unsigned int *err, int m0, int h, int kvh, int b,
+                         BlockRange br) {
+  using C = Cfg<D>;
+  mbar_arrive_expect_tx(&bars->q_full, kTiles * C::kTileBytes);
+  for (int t = 0; t < kTiles; ++t)
+    for (int c = 0; c < C::kChunks; ++c)
+      tma_load_4d(smem + C::kQOff + t * C::kTileBytes + c * C::kChunkBytes, tm_q, &bars->q_full, c * 64, h,
+                  m0 + t * kBM, b);
+  int issued_k = 0, issued_v = 0;
+  for (int j = 0; j < br.nb; ++j) {
+    const int s = j % C::kStages;
+    const uint32_t par = ((j / C::kStages) & 1) ^ 1;
+    const int n0 = br.n_start + j * kBN;
+    if (!mbar_wait(&bars->k_empty[s], par, kTimeoutNs)) {
+      set_abort(bars, err);
+      break;
+    }
+    mbar_arrive_expect_tx(&bars->k_full[s], C::kTileBytes);
+    for (int c = 0; c < C::kChunks; ++c)
+      tma_load_4d(smem + C::kKOff + s * C::kTileBytes + c * C::kChunkBytes, tm_k, &bars->k_full[s], c * 64, kvh,
+                  n0, b);
+    issued_k = j + 1;
+    if (!mbar_wait(&bars->v_empty[s], par, kTimeoutNs)) {
+      set_abort(bars, err);
+      break;
+    }
+    mbar_arrive_expect_tx(&bars->v_full[s], C::kTileBytes);
+    for (int c = 0; c < C::kChunks; ++c)
+      tma_load_4d(smem + C::kVOff + s * C::kTileBytes + c * C::kChunkBytes, tm_v, &bars->v_full[s], c * 64, kvh,
+                  n0, b);
+    issued_v = j + 1;
+    if (bars->abort_flag) break;
+  }
+  // Drain: every load issued must have landed before the CTA may exit.  In a
+  // normal run these phases completed long ago and the waits return at once.
+  mbar_wait(&bars->q_full, 0, kTimeoutNs);
+  for (int j = max(0, issued_k - C::kStages); j < issued_k; ++j)
+    mbar_wait(&bars->k_full[j % C::kStages], (j / C::kStages) & 1, kTimeoutNs);
+  for (int j = max(0, issued_v - C::kStages); j < issued_v; ++j)
+    mbar_wait(&bars->v_full[j % C::kStages], (j / C::kStages) & 1, kTimeoutNs);
+}
+
+// ---------------------------------------------------------------- MMA role
+template <int D, bool kBF16>
+__device__ void mma_role(uint8_t *smem, Bars *bars, unsigned int *err, uint32_t tmem, BlockRange br) {
+  using C = Cfg<D>;
+  constexpr uint32_t idesc_qk = idesc_f16(128, kBN, kBF16, false);
+  constexpr uint32_t idesc_pv = idesc_f16(128, D, kBF16, true);
+  const uint32_t q_base = smem_u32(smem + C::kQOff);
+  const uint32_t k_base = smem_u32(smem + C::kKOff);
+  const uint32_t v_base = smem_u32(smem + C::kVOff);
+
+  // S_t = Q_t K^T over D in steps of 16 (32 bytes inside a 128-byte chunk).
+  auto issue_qk = [&](int t, int s) {
+    const uint32_t d_tmem = tmem + (t ? C::kTmemS1 : C::kTmemS0);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const uint32_t koff = (kk / 4) * C::kChunkBytes + (kk % 4) * 32;
+      const uint64_t da = smem_desc_sw128(q_base + t * C::kTileBytes + koff, 16, 1024);
+      const uint64_t db = smem_desc_sw128(k_base + s * C::kTileBytes + koff, 16, 1024);
+      mma_ss(d_tmem, da, db, idesc_qk, kk > 0 ? 1u : 0u);
+    }
+  };
+  // O_t (+)= P_t V over the 128 keys in steps of 16 (P: 8 TMEM columns per
+  // step; V: 16 rows of 128 bytes per step, MN-major, 64-column chunks 16 KB apart).
+  auto issue_pv = [&](int t, int s, bool acc) {
+    const uint32_t d_tmem = tmem + (t ? C::kTmemO1 : C::kTmemO0);
+    const uint32_t p_tmem = tmem + (t ? C::kTmemS1 : C::kTmemS0);
+#pragma unroll
+    for (int kk = 0; kk < kBN / 16; ++kk) {
+      const uint64_t db = smem_desc_sw128(v_base + s * C::kTileBytes + kk * 16 * 128, C::kChunkBytes, 1024);
+      mma_ts(d_tmem, p_tmem + kk * 8, db, idesc_pv, (acc || kk > 0) ? 1u : 0u);
+    }
+  };
+
+  bool ok = mbar_wait(&bars->q_full, 0, kTimeoutNs) && mbar_wait(&bars->k_full[0], 0, kTimeoutNs);
+  if (!ok) set_abort(bars, err);
+  if (ok) {
+    tc_fence_after();
+    issue_qk(0, 0);
+    tc_commit(&bars->s_full[0]);
+    issue_qk(1, 0);
+    tc_commit(&bars->s_full[1]);
+    tc_commit(&bars->k_empty[0]);
+    for (int j = 0; j < br.nb; ++j) {
+      const int sv = j % C::kStages;
+      const int sk = (j + 1) % C::kStages;
+      const bool more = j + 1 < br.nb;
+      if (!mbar_wait(&bars->v_full[sv], (j / C::kStages) & 1, kTimeoutNs) ||
+          !mbar_wait(&bars->p_full[0], j & 1, kTimeoutNs)) {
+        set_abort(bars, err);
+        break;
+      }
+      tc_fence_after();
+      issue_pv(0, sv, j > 0);
+      tc_commit(&bars->o_done[0]);
+      if (more) {
+        if (!mbar_wait(&bars->k_full[sk], ((j + 1) / C::kStages) & 1, kTimeoutNs)) {
+          set_abort(bars, err);
+          break;
+        }
+        tc_fence_after();
+        issue_qk(0, sk);
+        tc_commit(&bars->s_full[0]);
+      }
+      if (!mbar_wait(&bars->p_full[1], j & 1, kTimeoutNs)) {
+        set_abort(bars, err);
+        break;
+      }
+      tc_fence_after();
+      issue_pv(1, sv, j > 0);
+      tc_commit(&bars->o_done[1]);
+      tc_commit(&bars->v_empty[sv]);
+      if (more) {
+        issue_qk(1, sk);
+        tc_commit(&bars->s_full[1]);
+        tc_commit(&bars->k_empty[sk]);
+      }
+      if (bars->abort_flag) break;
+    }
+  }
+  // Drain: all MMAs this thread issued complete before tensor memory is freed.
+  tc_commit(&bars->drain);
+  mbar_wait(&bars->drain, 0, kTimeoutNs);
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ------------------------------------------------------------ softmax role
+// Thread r of warpgroup t owns query row r of tile t (TMEM lane r).
+template <typename T, int D, bool kAlibi, bool kSoftcap>
+__device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int warp, BlockRange br, int m0,
+                             int h, int b, int ql, int kl) {
+  using C = Cfg<D>;
+  const float kNegInf = -CUDART_INF_F;
+  const int t = warp / 4;
+  const int r = threadIdx.x % kBM;
+  const int row0 = m0 + t * kBM;
+  const int qi = row0 + r;
+  const int off = kl - ql;
+  const int diag = qi + off;
+  const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
+  const uint32_t tS = tmem + lane_off + (t ? C::kTmemS1 : C::kTmemS0);
+  const uint32_t tO = tmem + lane_off + (t ? C::kTmemO1 : C::kTmemO0);
+  const float scale2 = a.sm_scale * kLog2e;
+  const float slope2 = kAlibi ? a.alibi[h] * kLog2e : 0.f;
+  const float cap_in = kSoftcap ? a.sm_scale / a.softcap : 0.f;
+  const float cap_out = kSoftcap ? a.softcap * kLog2e : 0.f;
+  float m_used = kNegInf, l = 0.f;
+  bool aborted = false;
+
+  for (int j = 0; j < br.nb; ++j) {
+    const int n0 = br.n_start + j * kBN;
+    bool ok = mbar_wait(&bars->s_full[t], j & 1, kTimeoutNs);
+    if (!__all_sync(0xffffffffu, ok)) {
+      set_abort(bars, a.err);
+      aborted = true;
+      break;
+    }
+    tc_fence_after();
+    uint32_t raw[4][32];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tmem_ld32(tS + q * 32, raw[q]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) reg_fence32(raw[q]);
+
+    // Per-element masking only on blocks that cross a boundary of this tile.
+    const bool need_mask = (n0 + kBN > kl) || (a.causal && n0 + kBN - 1 > row0 + off) ||
+                           (a.window >= 0 && row0 + kBM - 1 + off - n0 > a.window);
+    const float jf = (float)n0;
+    float sv[4][32];
+    float mx = kNegInf;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float v = __uint_as_float(raw[q][c]);
+        float y = kSoftcap ? tanhf(v * cap_in) * cap_out : v * scale2;
+        if (kAlibi) y = fmaf(slope2, jf + (float)(q * 32 + c), y);
+        if (need_mask) {
+          const int jj = n0 + q * 32 + c;
+          const bool vis = jj < kl && (!a.causal || jj <= diag) && (a.window < 0 || diag - jj <= a.window);
+          y = vis ? y : kNegInf;
+        }
+        sv[q][c] = y;
+        mx = fmaxf(mx, y);
+      }
+    }
+    const float m_new = fmaxf(m_used, mx);
+    float alpha = 1.f;
+    bool rescale = false;
+    if (m_used == kNegInf) {
+      m_used = m_new;  // nothing accumulated yet: O and l are zero
+    } else if (m_new > m_used + kRescaleThreshold) {
+      alpha = ex2_approx(m_used - m_new);
+      m_used = m_new;
+      rescale = true;
+    }
+    // P = 2^(s - m) rounded to the input type, two per TMEM column, written
+    // over the first 64 columns of S_t (already consumed into registers).
+    const float m_eff = (m_used == kNegInf) ? 0.f : m_used;
+    float psum = 0.f;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t pk[32];
+#pragma unroll
+      for (int c2 = 0; c2 < 32; ++c2) {
+        const int e = half * 64 + 2 * c2;
+        const float p0 = ex2_approx(sv[e / 32][e % 32] - m_eff);
+        const float p1 = ex2_approx(sv[(e + 1) / 32][(e + 1) % 32] - m_eff);
+        psum += p0 + p1;
+        pk[c2] = pack2<T>(p0, p1);
+      }
+      tmem_st32(tS + half * 32, pk);
+    }
+    l = l * alpha + psum;
+    if (__any_sync(0xffffffffu, rescale)) {
+      // O_t holds blocks 0..j-1 once PV_t(j-1) is done; rescale it in place.
+      ok = mbar_wait(&bars->o_done[t], (j - 1) & 1, kTimeoutNs);
+      if (!__all_sync(0xffffffffu, ok)) {
+        set_abort(bars, a.err);
+        aborted = true;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int ch = 0; ch < D / 32; ++ch) {
+        uint32_t o[32];
+        tmem_ld32(tO + ch * 32, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+        tmem_st32(tO + ch * 32, o);
+      }
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(&bars->p_full[t]);
+  }
+
+  // Epilogue: O_t / l -> global (rows past q_len as zeros), lse.
+  if (!aborted && br.nb > 0) {
+    bool ok = mbar_wait(&bars->o_done[t], (br.nb - 1) & 1, kTimeoutNs);
+    if (!__all_sync(0xffffffffu, ok)) {
+      set_abort(bars, a.err);
+      aborted = true;
+    } else {
+      tc_fence_after();
+    }
+  }
+  const bool have = !aborted && br.nb > 0;
+  const bool valid = qi < ql && l > 0.f;  // padded rows and rows with no visible key -> 0
+  const float inv = valid ? 1.f / l : 0.f;
+  T *orow = static_cast<T *>(a.o) + b * a.os[0] + (long long)qi * a.os[1] + h * a.os[2];
+#pragma unroll 1
+  for (int ch = 0; ch < D / 32; ++ch) {
+    uint32_t o[32];
+    if (have) {
+      tmem_ld32(tO + ch * 32, o);
+      tmem_wait_ld();
+      reg_fence32(o);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) o[c] = 0u;
+    }
+    uint32_t w[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      w[c] = valid ? pack2<T>(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv) : 0u;
+    if (qi < a.Sq) {
+      uint4 *dst = reinterpret_cast<uint4 *>(orow + ch * 32);
+#pragma unroll
+      for (int v4 = 0; v4 < 4; ++v4) dst[v4] = make_uint4(w[4 * v4], w[4 * v4 + 1], w[4 * v4 + 2], w[4 * v4 + 3]);
+    }
+  }
+  if (a.lse != nullptr && qi < a.Sq)
+    a.lse[((long long)b * a.H + h) * a.Sq + qi] = valid ? (m_used + log2f(l)) * kLn2 : kNegInf;
+}
+
+// ------------------------------------------------------------------ kernel
+template <typename T, int D, bool kAlibi, bool kSoftcap>
+__global__ void __launch_bounds__(kThreads, 1)
+    fmha_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int n_mblocks) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte swizzled tiles want 1024-byte aligned shared-memory addresses.
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars *bars = reinterpret_cast<Bars *>(smem + C::kBarOff);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // causal: the longest query blocks (highest rows) launch first
+  const int mblk = a.causal ? (n_mblocks - 1 - (int)blockIdx.x) : (int)blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z, kvh = h / a.group;
+  const int ql = clamp_len(a.q_lens, b, a.Sq);
+  const int kl = clamp_len(a.kv_lens, b, a.Skv);
+  const int m0 = mblk * (kTiles * kBM);
+  const BlockRange br = block_range(a, m0, ql, kl);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
+    }
+    for (int t = 0; t < kTiles; ++t) {
+      mbar_init(&bars->s_full[t], 1);
+      mbar_init(&bars->p_full[t], kBM);
+      mbar_init(&bars->o_done[t], 1);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kTmaWarp && lane == 0) {
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&bars->tmem_base, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == kTmaWarp) {
+    if (lane == 0 && br.nb > 0) tma_role<D>(&tm_q, &tm_k, &tm_v, smem, bars, a.err, m0, h, kvh, b, br);
+  } else if (warp == kMmaWarp) {
+    if (lane == 0 && br.nb > 0)
+      mma_role<D, std::is_same<T, __nv_bfloat16>::value>(smem, bars, a.err, tmem, br);
+  } else {
+    softmax_role<T, D, kAlibi, kSoftcap>(a, bars, tmem, warp, br, m0, h, b, ql, kl);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// -------------------------------------------------------------------- host
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Tensor map over a [B, S, H, D] tensor given element strides {batch, seq,
+// head}, dimensions ordered (D, H, S, B) innermost first, box 64 x 1 x 128 x 1
+// (one 128-byte column chunk of 128 rows), 128-byte swizzle, zero fill.
+bool make_tile_map(CUtensorMap *m, const void *base, bool bf16, int D, int S, int H, int B,
+                   const long long st[3]) {
+  EncodeTiledFn enc = encode_tiled();
+  if (enc == nullptr) return false;
+  // A dimension of extent 1 is never stepped along; give it any legal stride.
+  auto stride = [](long long elems, int extent) -> cuuint64_t {
+    cuuint64_t bytes = (cuuint64_t)elems * 2u;
+    if (extent <= 1 && (bytes == 0 || bytes % 16)) bytes = 16;
+    return bytes;
+  };
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {stride(st[2], H), stride(st[1], S), stride(st[0], B)};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <typename T, int D, bool kAlibi, bool kSoftcap>
+cudaError_t launch_t(const AttnArgs &a, cudaStream_t s) {
+  using C = Cfg<D>;
+  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  CUtensorMap tq, tk, tv;
+  if (!make_tile_map(&tq, a.q, bf16, D, a.Sq, a.H, a.B, a.qs) ||
+      !make_tile_map(&tk, a.k, bf16, D, a.Skv, a.Hkv, a.B, a.ks) ||
+      !make_tile_map(&tv, a.v, bf16, D, a.Skv, a.Hkv, a.B, a.vs))
+    return cudaErrorInvalidValue;
+  auto kern = fmha_sm100_kernel<T, D, kAlibi, kSoftcap>;
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  const int n_mblocks = (a.Sq + kTiles * kBM - 1) / (kTiles * kBM);
+  dim3 grid(n_mblocks, a.H, a.B);
+  kern<<<grid, kThreads, C::kSmemBytes, s>>>(tq, tk, tv, a, n_mblocks);
+  return cudaGetLastError();
+}
+
+template <typename T, int D>
+cudaError_t launch_d(const AttnArgs &a, cudaStream_t s) {
+  const bool alibi = a.alibi != nullptr, cap = a.softcap > 0.f;
+  if (alibi) return cap ? launch_t<T, D, true, true>(a, s) : launch_t<T, D, true, false>(a, s);
+  return cap ? launch_t<T, D, false, true>(a, s) : launch_t<T, D, false, false>(a, s);
+}
+
+}  // namespace
+
+bool sm100_supports(const AttnArgs &a) {
+  if (a.dtype != 1 && a.dtype != 2) return false;
+  if (a.D != 64 && a.D != 128) return false;
+  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al16(a.q) || !al16(a.k) || !al16(a.v) || !al16(a.o)) return false;
+  const long long *st[4] = {a.qs, a.ks, a.vs, a.os};
+  for (int t = 0; t < 4; ++t)
+    for (int i = 0; i < 3; ++i)
+      if (st[t][i] % 8) return false;  // 16-byte strides (TMA, vector stores)
+  return true;
+}
+
+cudaError_t launch_sm100(const AttnArgs &a, cudaStream_t s) {
+  if (!sm100_supports(a)) return cudaErrorNotSupported;
+  if (a.dtype == 1) return a.D == 64 ? launch_d<__half, 64>(a, s) : launch_d<__half, 128>(a, s);
+  return a.D == 64 ? launch_d<__nv_bfloat16, 64>(a, s) : launch_d<__nv_bfloat16, 128>(a, s);
+}
+
 }  // namespace llmx_b200

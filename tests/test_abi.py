@@ -115,6 +115,7 @@ def test_negative_stride_rejected():
 
 
 def test_algorithm_selection():
+    assert _select(_params()) == (0, _lib.ALGO["tcgen05"])
     assert _select(_params(max_q_len=1)) == (0, _lib.ALGO["decode"])
     assert _select(_params(dtype=0)) == (0, _lib.ALGO["simt"])
     assert _select(_params(head_dim=80)) == (0, _lib.ALGO["simt"])
