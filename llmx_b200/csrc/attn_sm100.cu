@@ -255,6 +255,54 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Score of column c (0..127 inside the block) in log2 units, before masking.
+template <bool kAlibi, bool kSoftcap>
+__device__ __forceinline__ float score2(uint32_t raw, int c, float scale2, float slope2, float jf, float cap_in,
+                                        float cap_out) {
+  const float v = __uint_as_float(raw);
+  float y = kSoftcap ? tanhf(v * cap_in) * cap_out : v * scale2;
+  if (kAlibi) y = fmaf(slope2, (float)c, fmaf(slope2, jf, y));
+  return y;
+}
+
+// Max of 32 scores (columns c0..c0+31), four independent chains.
+template <bool kAlibi, bool kSoftcap, bool kMask>
+__device__ __forceinline__ float chunk_max(const uint32_t (&v)[32], int c0, int lo, int hi, float scale2,
+                                           float slope2, float jf, float cap_in, float cap_out) {
+  float m[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m[i] = -CUDART_INF_F;
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    float y = score2<kAlibi, kSoftcap>(v[c], c0 + c, scale2, slope2, jf, cap_in, cap_out);
+    if (kMask) y = (c0 + c >= lo && c0 + c < hi) ? y : -CUDART_INF_F;
+    m[c & 3] = fmaxf(m[c & 3], y);
+  }
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
+// p = 2^(score - m) for 32 columns, packed in pairs into pk[k0 .. k0+15];
+// returns the sum of the unrounded p (four independent chains).
+template <typename T, bool kAlibi, bool kSoftcap, bool kMask>
+__device__ __forceinline__ float chunk_exp(const uint32_t (&v)[32], uint32_t (&pk)[32], int k0, int c0, int lo,
+                                           int hi, float scale2, float slope2, float jf, float cap_in,
+                                           float cap_out, float m) {
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    float y0 = score2<kAlibi, kSoftcap>(v[c], c0 + c, scale2, slope2, jf, cap_in, cap_out);
+    float y1 = score2<kAlibi, kSoftcap>(v[c + 1], c0 + c + 1, scale2, slope2, jf, cap_in, cap_out);
+    if (kMask) {
+      y0 = (c0 + c >= lo && c0 + c < hi) ? y0 : -CUDART_INF_F;
+      y1 = (c0 + c + 1 >= lo && c0 + c + 1 < hi) ? y1 : -CUDART_INF_F;
+    }
+    const float p0 = ex2_approx(y0 - m), p1 = ex2_approx(y1 - m);
+    s[(c >> 1) & 3] += p0 + p1;
+    pk[k0 + c / 2] = pack2<T>(p0, p1);
+  }
+  return (s[0] + s[1]) + (s[2] + s[3]);
+}
+
 // ------------------------------------------------------------ softmax role
 // Thread r of warpgroup t owns query row r of tile t (TMEM lane r).
 template <typename T, int D, bool kAlibi, bool kSoftcap>
@@ -287,33 +335,37 @@ __device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
       break;
     }
     tc_fence_after();
-    uint32_t raw[4][32];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) tmem_ld32(tS + q * 32, raw[q]);
-    tmem_wait_ld();
-#pragma unroll
-    for (int q = 0; q < 4; ++q) reg_fence32(raw[q]);
-
-    // Per-element masking only on blocks that cross a boundary of this tile.
+    // Visible keys of this row inside the block form one interval [lo, hi)
+    // (bottom-right causal and length bound cut above, the window below).
+    int lo = 0, hi = kBN;
     const bool need_mask = (n0 + kBN > kl) || (a.causal && n0 + kBN - 1 > row0 + off) ||
                            (a.window >= 0 && row0 + kBM - 1 + off - n0 > a.window);
+    if (need_mask) {
+      hi = min(kBN, kl - n0);
+      if (a.causal) hi = min(hi, diag - n0 + 1);
+      if (a.window >= 0) lo = max(0, diag - a.window - n0);
+    }
     const float jf = (float)n0;
-    float sv[4][32];
+    // An opaque per-block copy of the slope keeps the compiler from hoisting
+    // 128 per-column products slope * c out of the block loop into registers.
+    float sl = slope2;
+    asm volatile("" : "+f"(sl));
+    // Pass 1: row max over the block, 32 columns at a time (two loads in flight).
     float mx = kNegInf;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float v = __uint_as_float(raw[q][c]);
-        float y = kSoftcap ? tanhf(v * cap_in) * cap_out : v * scale2;
-        if (kAlibi) y = fmaf(slope2, jf + (float)(q * 32 + c), y);
-        if (need_mask) {
-          const int jj = n0 + q * 32 + c;
-          const bool vis = jj < kl && (!a.causal || jj <= diag) && (a.window < 0 || diag - jj <= a.window);
-          y = vis ? y : kNegInf;
-        }
-        sv[q][c] = y;
-        mx = fmaxf(mx, y);
+    for (int half = 0; half < 2; ++half) {
+      uint32_t b0[32], b1[32];
+      tmem_ld32(tS + half * 64, b0);
+      tmem_ld32(tS + half * 64 + 32, b1);
+      tmem_wait_ld();
+      reg_fence32(b0);
+      reg_fence32(b1);
+      if (need_mask) {
+        mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, true>(b0, half * 64, lo, hi, scale2, sl, jf, cap_in, cap_out));
+        mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, true>(b1, half * 64 + 32, lo, hi, scale2, sl, jf, cap_in, cap_out));
+      } else {
+        mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, false>(b0, half * 64, lo, hi, scale2, sl, jf, cap_in, cap_out));
+        mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, false>(b1, half * 64 + 32, lo, hi, scale2, sl, jf, cap_in, cap_out));
       }
     }
     const float m_new = fmaxf(m_used, mx);
@@ -326,20 +378,29 @@ __device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
       m_used = m_new;
       rescale = true;
     }
-    // P = 2^(s - m) rounded to the input type, two per TMEM column, written
-    // over the first 64 columns of S_t (already consumed into registers).
+    // Pass 2: P = 2^(s - m) rounded to the input type, two per TMEM column,
+    // written over S_t columns that pass 2 has already read.  The scores are
+    // recomputed from TMEM; hiding jf from the optimiser keeps it from
+    // carrying 128 per-column bias terms across the passes in registers.
     const float m_eff = (m_used == kNegInf) ? 0.f : m_used;
+    float jf2 = jf, sl2 = slope2;
+    asm volatile("" : "+f"(jf2), "+f"(sl2));
     float psum = 0.f;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
+      uint32_t b0[32], b1[32];
+      tmem_ld32(tS + half * 64, b0);
+      tmem_ld32(tS + half * 64 + 32, b1);
+      tmem_wait_ld();
+      reg_fence32(b0);
+      reg_fence32(b1);
       uint32_t pk[32];
-#pragma unroll
-      for (int c2 = 0; c2 < 32; ++c2) {
-        const int e = half * 64 + 2 * c2;
-        const float p0 = ex2_approx(sv[e / 32][e % 32] - m_eff);
-        const float p1 = ex2_approx(sv[(e + 1) / 32][(e + 1) % 32] - m_eff);
-        psum += p0 + p1;
-        pk[c2] = pack2<T>(p0, p1);
+      if (need_mask) {
+        psum += chunk_exp<T, kAlibi, kSoftcap, true>(b0, pk, 0, half * 64, lo, hi, scale2, sl2, jf2, cap_in, cap_out, m_eff);
+        psum += chunk_exp<T, kAlibi, kSoftcap, true>(b1, pk, 16, half * 64 + 32, lo, hi, scale2, sl2, jf2, cap_in, cap_out, m_eff);
+      } else {
+        psum += chunk_exp<T, kAlibi, kSoftcap, false>(b0, pk, 0, half * 64, lo, hi, scale2, sl2, jf2, cap_in, cap_out, m_eff);
+        psum += chunk_exp<T, kAlibi, kSoftcap, false>(b1, pk, 16, half * 64 + 32, lo, hi, scale2, sl2, jf2, cap_in, cap_out, m_eff);
       }
       tmem_st32(tS + half * 32, pk);
     }

@@ -43,27 +43,31 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+// One bounded sleep on the phase: the thread is suspended until the phase
+// with parity `parity` completes or `hint_ns` passes, whichever is first.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
 
 // Waits for the phase of `bar` with parity `parity` to complete, for at most
 // `timeout_ns`.  Returns false on timeout (the caller records the error and
-// unwinds); never spins forever.
+// unwinds); never spins forever.  Waiting threads sleep in try_wait instead
+// of spinning, so they take no issue slots from the warps doing the work.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+  constexpr uint32_t kSleepNs = 100000;
+  if (mbar_try_wait(bar, parity, kSleepNs)) return true;
   const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0 && global_timer_ns() - t0 > timeout_ns) return false;
+  for (;;) {
+    if (mbar_try_wait(bar, parity, kSleepNs)) return true;
+    if (global_timer_ns() - t0 > timeout_ns) return false;
   }
 }
 
