@@ -13,11 +13,12 @@
 // type before PV (single_mha_kernel.cuh:232-233), GQA head h -> kv head
 // h / group.
 //
-// CTA = 2 query tiles of 128 rows of one (batch, head); 10 warps:
-//   warps 0-3  softmax for query tile 0 (thread r owns row r = TMEM lane r)
-//   warps 4-7  softmax for query tile 1
-//   warp  8    tensor-memory allocation + MMA issue (one thread)
-//   warp  9    TMA producer (one thread)
+// CTA = 2 query tiles of 128 rows of one (batch, head); 12 warps:
+//   warps 0-3   softmax for query tile 0 (thread r owns row r = TMEM lane r)
+//   warps 4-7   softmax for query tile 1
+//   warp  8     tensor-memory allocation + MMA issue (one thread)
+//   warp  9     TMA producer (one thread)
+//   warps 10-11 idle (they complete the third warpgroup for setmaxnreg)
 // Tensor memory (512 columns x 128 lanes of 32 bit):
 //   [0,128) S0 / P0, [128,256) S1 / P1, [256,256+D) O0, [256+D,256+2D) O1.
 // P (16-bit, two per column) overwrites the first 64 columns of its S.
@@ -51,9 +52,15 @@ using namespace sm100;
 constexpr int kBM = 128;       // query rows per tile
 constexpr int kTiles = 2;      // query tiles per CTA
 constexpr int kBN = 128;       // keys per KV block
-constexpr int kThreads = 320;  // 8 softmax warps + MMA warp + TMA warp
+constexpr int kThreads = 384;  // 2 softmax warpgroups + MMA / TMA warpgroup
 constexpr int kMmaWarp = 8;
 constexpr int kTmaWarp = 9;
+// Register split (setmaxnreg): the CTA launches with 384 x 168; the MMA / TMA
+// warpgroup gives back down to 80 and the softmax warpgroups grow to 208:
+// 128 * 80 + 256 * 208 = 63488 <= 384 * 168 = 64512.
+constexpr uint32_t kRegsControl = 80;
+constexpr uint32_t kRegsSoftmax = 208;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * 168, "register split exceeds the launch");
 constexpr uint64_t kTimeoutNs = 1000000000ull;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -281,12 +288,12 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&v)[32], int c0, int 
   return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
 }
 
-// p = 2^(score - m) for 32 columns, packed in pairs into pk[k0 .. k0+15];
+// p = 2^(score - m) for 32 columns, packed in pairs into pk[0..15];
 // returns the sum of the unrounded p (four independent chains).
 template <typename T, bool kAlibi, bool kSoftcap, bool kMask>
-__device__ __forceinline__ float chunk_exp(const uint32_t (&v)[32], uint32_t (&pk)[32], int k0, int c0, int lo,
-                                           int hi, float scale2, float slope2, float jf, float cap_in,
-                                           float cap_out, float m) {
+__device__ __forceinline__ float chunk_exp(const uint32_t (&v)[32], uint32_t (&pk)[16], int c0, int lo, int hi,
+                                           float scale2, float slope2, float jf, float cap_in, float cap_out,
+                                           float m) {
   float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int c = 0; c < 32; c += 2) {
@@ -298,9 +305,56 @@ __device__ __forceinline__ float chunk_exp(const uint32_t (&v)[32], uint32_t (&p
     }
     const float p0 = ex2_approx(y0 - m), p1 = ex2_approx(y1 - m);
     s[(c >> 1) & 3] += p0 + p1;
-    pk[k0 + c / 2] = pack2<T>(p0, p1);
+    pk[c / 2] = pack2<T>(p0, p1);
   }
   return (s[0] + s[1]) + (s[2] + s[3]);
+}
+
+// One KV block of one row: load S (128 columns, one TMEM round trip), row
+// max, the rescale decision, P = 2^(s - m) written back over S as 16-bit
+// pairs, and the running sum.  kMask selects the per-column interval test;
+// the two variants are separate code paths.
+template <typename T, bool kAlibi, bool kSoftcap, bool kMask>
+__device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int lo, int hi, float scale2, float slope2,
+                                              float cap_in, float cap_out, float &m_used, float &l, float &alpha,
+                                              bool &rescale) {
+  const float kNegInf = -CUDART_INF_F;
+  const float jf = (float)n0;
+  // An opaque per-block copy of the slope keeps the compiler from hoisting
+  // 128 per-column products slope * c out of the block loop into registers.
+  float sl = slope2;
+  asm volatile("" : "+f"(sl));
+  uint32_t sr[4][32];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) tmem_ld32(tS + q * 32, sr[q]);
+  tmem_wait_ld();
+#pragma unroll
+  for (int q = 0; q < 4; ++q) reg_fence32(sr[q]);
+  float mx = kNegInf;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, kMask>(sr[q], q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out));
+  // Fresh names for the raw scores: pass 2 recomputes each transformed
+  // score instead of keeping pass 1's values alive next to the raw row.
+#pragma unroll
+  for (int q = 0; q < 4; ++q) reg_fence32(sr[q]);
+  const float m_new = fmaxf(m_used, mx);
+  if (m_used == kNegInf) {
+    m_used = m_new;  // nothing accumulated yet: O and l are zero
+  } else if (m_new > m_used + kRescaleThreshold) {
+    alpha = ex2_approx(m_used - m_new);
+    m_used = m_new;
+    rescale = true;
+  }
+  const float m_eff = (m_used == kNegInf) ? 0.f : m_used;
+  float psum = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t pk[16];
+    psum += chunk_exp<T, kAlibi, kSoftcap, kMask>(sr[q], pk, q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out, m_eff);
+    tmem_st16(tS + q * 16, pk);
+  }
+  l = l * alpha + psum;
 }
 
 // ------------------------------------------------------------ softmax role
@@ -345,66 +399,14 @@ __device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
       if (a.causal) hi = min(hi, diag - n0 + 1);
       if (a.window >= 0) lo = max(0, diag - a.window - n0);
     }
-    const float jf = (float)n0;
-    // An opaque per-block copy of the slope keeps the compiler from hoisting
-    // 128 per-column products slope * c out of the block loop into registers.
-    float sl = slope2;
-    asm volatile("" : "+f"(sl));
-    // Pass 1: row max over the block, 32 columns at a time (two loads in flight).
-    float mx = kNegInf;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t b0[32], b1[32];
-      tmem_ld32(tS + half * 64, b0);
-      tmem_ld32(tS + half * 64 + 32, b1);
-      tmem_wait_ld();
-      reg_fence32(b0);
-      reg_fence32(b1);
-      if (need_mask) {
-        mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, true>(b0, half * 64, lo, hi, scale2, sl, jf, cap_in, cap_out));
-        mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, true>(b1, half * 64 + 32, lo, hi, scale2, sl, jf, cap_in, cap_out));
-      } else {
-        mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, false>(b0, half * 64, lo, hi, scale2, sl, jf, cap_in, cap_out));
-        mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, false>(b1, half * 64 + 32, lo, hi, scale2, sl, jf, cap_in, cap_out));
-      }
-    }
-    const float m_new = fmaxf(m_used, mx);
     float alpha = 1.f;
     bool rescale = false;
-    if (m_used == kNegInf) {
-      m_used = m_new;  // nothing accumulated yet: O and l are zero
-    } else if (m_new > m_used + kRescaleThreshold) {
-      alpha = ex2_approx(m_used - m_new);
-      m_used = m_new;
-      rescale = true;
-    }
-    // Pass 2: P = 2^(s - m) rounded to the input type, two per TMEM column,
-    // written over S_t columns that pass 2 has already read.  The scores are
-    // recomputed from TMEM; hiding jf from the optimiser keeps it from
-    // carrying 128 per-column bias terms across the passes in registers.
-    const float m_eff = (m_used == kNegInf) ? 0.f : m_used;
-    float jf2 = jf, sl2 = slope2;
-    asm volatile("" : "+f"(jf2), "+f"(sl2));
-    float psum = 0.f;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t b0[32], b1[32];
-      tmem_ld32(tS + half * 64, b0);
-      tmem_ld32(tS + half * 64 + 32, b1);
-      tmem_wait_ld();
-      reg_fence32(b0);
-      reg_fence32(b1);
-      uint32_t pk[32];
-      if (need_mask) {
-        psum += chunk_exp<T, kAlibi, kSoftcap, true>(b0, pk, 0, half * 64, lo, hi, scale2, sl2, jf2, cap_in, cap_out, m_eff);
-        psum += chunk_exp<T, kAlibi, kSoftcap, true>(b1, pk, 16, half * 64 + 32, lo, hi, scale2, sl2, jf2, cap_in, cap_out, m_eff);
-      } else {
-        psum += chunk_exp<T, kAlibi, kSoftcap, false>(b0, pk, 0, half * 64, lo, hi, scale2, sl2, jf2, cap_in, cap_out, m_eff);
-        psum += chunk_exp<T, kAlibi, kSoftcap, false>(b1, pk, 16, half * 64 + 32, lo, hi, scale2, sl2, jf2, cap_in, cap_out, m_eff);
-      }
-      tmem_st32(tS + half * 32, pk);
-    }
-    l = l * alpha + psum;
+    if (need_mask)
+      softmax_block<T, kAlibi, kSoftcap, true>(tS, n0, lo, hi, scale2, slope2, cap_in, cap_out, m_used, l, alpha,
+                                               rescale);
+    else
+      softmax_block<T, kAlibi, kSoftcap, false>(tS, n0, lo, hi, scale2, slope2, cap_in, cap_out, m_used, l, alpha,
+                                                rescale);
     if (__any_sync(0xffffffffu, rescale)) {
       // O_t holds blocks 0..j-1 once PV_t(j-1) is done; rescale it in place.
       ok = mbar_wait(&bars->o_done[t], (j - 1) & 1, kTimeoutNs);
@@ -519,12 +521,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == kTmaWarp) {
-    if (lane == 0 && br.nb > 0) tma_role<D>(&tm_q, &tm_k, &tm_v, smem, bars, a.err, m0, h, kvh, b, br);
-  } else if (warp == kMmaWarp) {
-    if (lane == 0 && br.nb > 0)
-      mma_role<D, std::is_same<T, __nv_bfloat16>::value>(smem, bars, a.err, tmem, br);
+  if (warp >= 8) {
+    regs_decrease<kRegsControl>();
+    if (warp == kTmaWarp) {
+      if (lane == 0 && br.nb > 0) tma_role<D>(&tm_q, &tm_k, &tm_v, smem, bars, a.err, m0, h, kvh, b, br);
+    } else if (warp == kMmaWarp) {
+      if (lane == 0 && br.nb > 0)
+        mma_role<D, std::is_same<T, __nv_bfloat16>::value>(smem, bars, a.err, tmem, br);
+    }
   } else {
+    regs_increase<kRegsSoftmax>();
     softmax_role<T, D, kAlibi, kSoftcap>(a, bars, tmem, warp, br, m0, h, b, ql, kl);
   }
 
