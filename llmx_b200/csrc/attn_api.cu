@@ -16,7 +16,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/llmx_attn.h"
+#include "llmx_attn.h"
 #include "attn_internal.h"
 
 namespace llmx_b200 {

@@ -39,6 +39,7 @@
 // for its in-flight TMA loads and MMAs, frees tensor memory and exits.
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -272,6 +273,13 @@ __device__ __forceinline__ float score2(uint32_t raw, int c, float scale2, float
   return y;
 }
 
+// Three-input max (sm_100 max.f32 with three sources).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Max of 32 scores (columns c0..c0+31), four independent chains.
 template <bool kAlibi, bool kSoftcap, bool kMask>
 __device__ __forceinline__ float chunk_max(const uint32_t (&v)[32], int c0, int lo, int hi, float scale2,
@@ -280,10 +288,14 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&v)[32], int c0, int 
 #pragma unroll
   for (int i = 0; i < 4; ++i) m[i] = -CUDART_INF_F;
 #pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    float y = score2<kAlibi, kSoftcap>(v[c], c0 + c, scale2, slope2, jf, cap_in, cap_out);
-    if (kMask) y = (c0 + c >= lo && c0 + c < hi) ? y : -CUDART_INF_F;
-    m[c & 3] = fmaxf(m[c & 3], y);
+  for (int c = 0; c < 32; c += 2) {
+    float y0 = score2<kAlibi, kSoftcap>(v[c], c0 + c, scale2, slope2, jf, cap_in, cap_out);
+    float y1 = score2<kAlibi, kSoftcap>(v[c + 1], c0 + c + 1, scale2, slope2, jf, cap_in, cap_out);
+    if (kMask) {
+      y0 = (c0 + c >= lo && c0 + c < hi) ? y0 : -CUDART_INF_F;
+      y1 = (c0 + c + 1 >= lo && c0 + c + 1 < hi) ? y1 : -CUDART_INF_F;
+    }
+    m[(c >> 1) & 3] = fmax3(m[(c >> 1) & 3], y0, y1);
   }
   return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
 }
@@ -475,16 +487,30 @@ __device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
 template <typename T, int D, bool kAlibi, bool kSoftcap>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int n_mblocks) {
+                      const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int n_mblocks,
+                      const int group_units) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzled tiles want 1024-byte aligned shared-memory addresses.
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars *bars = reinterpret_cast<Bars *>(smem + C::kBarOff);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // causal: the longest query blocks (highest rows) launch first
-  const int mblk = a.causal ? (n_mblocks - 1 - (int)blockIdx.x) : (int)blockIdx.x;
-  const int h = blockIdx.y, b = blockIdx.z, kvh = h / a.group;
+  // Work order: (batch, head) units in groups of `group_units` whose K/V fit
+  // in L2 together; inside a group the query blocks go longest first (with
+  // causal masking the highest rows see the most keys), so the machine works
+  // on one L2-resident K/V set at a time and short blocks fill the tail.
+  int mblk, unit;
+  {
+    const int units = a.B * a.H;
+    const int per_group = group_units * n_mblocks;
+    const int g = (int)blockIdx.x / per_group;
+    const int within = (int)blockIdx.x - g * per_group;
+    const int gu = min(group_units, units - g * group_units);
+    const int rank = within / gu;
+    unit = g * group_units + within % gu;
+    mblk = a.causal ? (n_mblocks - 1 - rank) : rank;
+  }
+  const int h = unit % a.H, b = unit / a.H, kvh = h / a.group;
   const int ql = clamp_len(a.q_lens, b, a.Sq);
   const int kl = clamp_len(a.kv_lens, b, a.Skv);
   const int m0 = mblk * (kTiles * kBM);
@@ -602,9 +628,15 @@ cudaError_t launch_t(const AttnArgs &a, cudaStream_t s) {
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   });
   if (attr_err != cudaSuccess) return attr_err;
-  const int n_mblocks = (a.Sq + kTiles * kBM - 1) / (kTiles * kBM);
-  dim3 grid(n_mblocks, a.H, a.B);
-  kern<<<grid, kThreads, C::kSmemBytes, s>>>(tq, tk, tv, a, n_mblocks);
+  const long long n_mblocks = (a.Sq + kTiles * kBM - 1) / (kTiles * kBM);
+  const long long units = (long long)a.B * a.H;
+  if (n_mblocks * units > 0x7fffffffLL) return cudaErrorInvalidValue;
+  // Units per group: K and V rows of one unit take Skv * D * 4 bytes; keep a
+  // group's K/V within about half of the 126 MB L2.
+  const long long kv_unit = std::max<long long>(1, (long long)a.Skv * D * 4);
+  const int group_units = (int)std::max<long long>(1, std::min<long long>(units, (64ll << 20) / kv_unit));
+  dim3 grid((unsigned)(n_mblocks * units));
+  kern<<<grid, kThreads, C::kSmemBytes, s>>>(tq, tk, tv, a, (int)n_mblocks, group_units);
   return cudaGetLastError();
 }
 
