@@ -286,6 +286,43 @@ def bench_workload(name, steps, warmup, rank, world, device, stream, peaks, with
     return res, w, inp
 
 
+def bench_kv_split(steps, warmup, rank, world, device, stream, peaks):
+    """Long-context prefill with its keys split over all ranks (zig-zag chunks,
+    NCCL log-sum-exp merge); strong scaling: the job is one fixed sequence."""
+    import torch.distributed as dist
+
+    from llmx_b200 import parallel
+    from llmx_b200.workloads import WORKLOADS, flops, make_inputs
+
+    w = WORKLOADS["long_prefill_bf16_b1_h32_s32768_d128"]
+    inp = make_inputs(w, device)
+    S = w.q_len
+    chunks = parallel.zigzag_chunks(S, world, rank)
+    kc = [inp.k[:, a:b] for a, b in chunks]
+    vc = [inp.v[:, a:b] for a, b in chunks]
+    offs = [a for a, _ in chunks]
+    times = []
+    with torch.cuda.stream(stream):
+        for i in range(warmup + steps):
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            parallel.kv_split_attention(inp.q, kc, vc, offs, S, w.sm_scale, alibi_slopes=inp.alibi)
+            e1.record(stream)
+            if i >= warmup:
+                times.append((e0, e1))
+    stream.synchronize()
+    ms = torch.tensor([sum(a.elapsed_time(b) for a, b in times)], dtype=torch.float64, device=device)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    per = float(ms.item()) / steps
+    fl = flops(w, [S], [S])
+    return {"kernel": "tcgen05 + NCCL lse merge", "value": fl / (per * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": per, "scaling": "strong", "chunks_per_rank": len(chunks),
+            "roofline": {"bound": "tensor", "achieved": fl / world / (per * 1e-3) / 1e12,
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s per GPU",
+                         "frac": fl / world / (per * 1e-3) / 1e12 / peaks["bf16_tflops"]}}
+
+
 def run_ours(args):
     rank, world, local = dist_info()
     device = torch.device("cuda", local)
@@ -312,6 +349,9 @@ def run_ours(args):
             r, _, _ = bench_workload(name, steps, min(args.warmup, 3) if name.startswith("long_") else args.warmup,
                                      rank, world, device, stream, peaks, False)
             extras[name] = {k: r[k] for k in ("kernel", "value", "unit", "ms_per_step", "roofline")}
+    if world > 1 and not args.no_extra:
+        extras["long_prefill_kv_split_" + str(world) + "gpu"] = bench_kv_split(
+            3, min(args.warmup, 3), rank, world, device, stream, peaks)
     cpu = None
     if rank == 0 and world == 1:
         sample = cpu_units_sample(w, inp, args.cpu_units)

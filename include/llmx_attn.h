@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define LLMX_ATTN_ABI_VERSION 1
+#define LLMX_ATTN_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define LLMX_API __attribute__((visibility("default")))
@@ -71,6 +71,7 @@ typedef enum llmx_attn_algo {
  * (params.h:35-50), then + alibi_slopes[h] * j (mask.h:75-77).
  * Query rows past q_len_b and rows that see no key are written as 0 (their
  * lse as -inf).  GQA: head h reads kv head h / (n_heads / n_kv_heads).
+ * With kv_offset / kv_total (below) j is the key's global position.
  */
 typedef struct llmx_attn_params {
   int32_t dtype;      /* llmx_dtype of q, k, v and o                    */
@@ -99,6 +100,12 @@ typedef struct llmx_attn_params {
   float *lse;                 /* NULL or device [batch, n_heads, max_q_len] fp32 */
   void *workspace;            /* device scratch for split-KV partials    */
   size_t workspace_bytes;
+  /* Key shards (a sequence's keys split across calls or GPUs): local key j
+   * sits at global position kv_offset + j, and the causal / window diagonal
+   * of query row i is i + (kv_total - q_len_b) (kv_total <= 0: the local
+   * kv_len_b).  ALiBi uses the global position.  Both 0 for unsharded keys. */
+  int32_t kv_offset;
+  int32_t kv_total;
 } llmx_attn_params;
 
 /* Fills *p with defaults: contiguous-stride fields zero, causal = 1,

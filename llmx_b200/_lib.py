@@ -60,6 +60,8 @@ class AttnParams(ctypes.Structure):
         ("lse", _vp),
         ("workspace", _vp),
         ("workspace_bytes", ctypes.c_size_t),
+        ("kv_offset", _i32),
+        ("kv_total", _i32),
     ]
 
 

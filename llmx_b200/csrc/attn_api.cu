@@ -112,6 +112,8 @@ llmx_status validate(const llmx_attn_params *p, AttnArgs *a) {
     return fail(LLMX_ERR_INVALID_ARGUMENT, "logits_soft_cap must be finite");
   if (p->algo < LLMX_ALGO_AUTO || p->algo > LLMX_ALGO_TCGEN05)
     return fail(LLMX_ERR_INVALID_ARGUMENT, "unknown algo");
+  if (p->kv_offset < 0 || p->kv_total < 0)
+    return fail(LLMX_ERR_INVALID_ARGUMENT, "kv_offset and kv_total must be >= 0");
   const int64_t *st[4] = {p->q_stride, p->k_stride, p->v_stride, p->o_stride};
   for (int t = 0; t < 4; ++t)
     for (int i = 0; i < 3; ++i)
@@ -142,6 +144,8 @@ llmx_status validate(const llmx_attn_params *p, AttnArgs *a) {
   a->causal = p->causal ? 1 : 0;
   a->window = p->sliding_window < 0 ? -1 : p->sliding_window;
   a->lse = p->lse;
+  a->kv_offset = p->kv_offset;
+  a->kv_total = p->kv_total;
   a->err = nullptr;
   a->num_sms = 148;
   return LLMX_OK;

@@ -57,9 +57,13 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(AttnArgs a, int 
   const int kl = ql > 0 ? clamp_len(a.kv_lens, b, a.Skv) : 0;
   const int k_begin = split * chunk;
   if (split > 0 && k_begin >= kl) return;  // nothing here; the combine skips it
+  // The single query row sits on diagonal doff (local key index): causal
+  // keys j <= doff, window keys j >= doff - window (mask.h:54-66).
+  const int doff = diag_shift(a, 1, kl);
   int k_end = min(kl, k_begin + chunk);
+  if (a.causal) k_end = min(k_end, max(k_begin, doff + 1));
   int k_lo = k_begin;
-  if (a.window >= 0) k_lo = max(k_lo, kl - 1 - a.window);  // (kl-1) - j <= window
+  if (a.window >= 0) k_lo = max(k_lo, doff - a.window);
 
   const int head0 = kvh * a.group + hg * GP;
   const int n_valid_heads = min(GP, a.group - hg * GP);
@@ -130,7 +134,7 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(AttnArgs a, int 
         } else {
           sc = d * scale2;
         }
-        sc += slope[g] * (float)kj[u];
+        sc += slope[g] * (float)(kj[u] + a.kv_offset);
         s[u][g] = vis ? sc : -CUDART_INF_F;
       }
     }

@@ -31,6 +31,8 @@ struct AttnArgs {
   int causal;
   int window;  // < 0: off
   float *lse;  // nullable [B, H, Sq]
+  int kv_offset;  // global position of local key 0
+  int kv_total;   // full key length for the causal / window diagonal (0: local)
   unsigned int *err;  // device error word (never null)
   int num_sms;
 };

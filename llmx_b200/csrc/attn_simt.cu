@@ -70,11 +70,12 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a) {
   }
 
   // Key range that any row of this tile can see.
+  const int doff = diag_shift(a, ql, kl);
   const int r_last = min(q0 + kBM, ql) - 1;
   int lo = 0, hi = kl;
   if (q0 < ql) {
-    if (a.causal) hi = min(kl, r_last + (kl - ql) + 1);
-    if (a.window >= 0) lo = max(0, q0 + (kl - ql) - a.window);
+    if (a.causal) hi = max(0, min(kl, r_last + doff + 1));
+    if (a.window >= 0) lo = min(kl, max(0, q0 + doff - a.window));
   } else {
     hi = 0;
   }
@@ -103,12 +104,12 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a) {
       const int r = e / kBN, c = e % kBN;
       const int i = q0 + r, j = n0 + c;
       float s = -CUDART_INF_F;
-      if (i < ql && key_visible(i, j, ql, kl, a.causal, a.window)) {
+      if (i < ql && key_visible(i, j, kl, doff, a.causal, a.window)) {
         float dot = 0.f;
         const float *qr = Qs + r * DMAX;
         const float *kr = Ks + c * (DMAX + 1);
         for (int d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
-        s = score_transform(dot, a.sm_scale, a.softcap, slope, j);
+        s = score_transform(dot, a.sm_scale, a.softcap, slope, j + a.kv_offset);
       }
       Ss[e] = s;
     }

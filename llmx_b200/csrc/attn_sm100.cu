@@ -116,7 +116,7 @@ struct BlockRange {
 __device__ __forceinline__ BlockRange block_range(const AttnArgs &a, int m0, int ql, int kl) {
   BlockRange r{0, 0};
   if (m0 >= ql || kl <= 0) return r;
-  const int off = kl - ql;
+  const int off = diag_shift(a, ql, kl);
   const int r_last = min(m0 + kTiles * kBM, ql) - 1;
   const int hi = a.causal ? min(kl, r_last + off + 1) : kl;
   int lo = a.window >= 0 ? max(0, m0 + off - a.window) : 0;
@@ -327,11 +327,12 @@ __device__ __forceinline__ float chunk_exp(const uint32_t (&v)[32], uint32_t (&p
 // pairs, and the running sum.  kMask selects the per-column interval test;
 // the two variants are separate code paths.
 template <typename T, bool kAlibi, bool kSoftcap, bool kMask>
-__device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int lo, int hi, float scale2, float slope2,
+__device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int kv_offset, int lo, int hi, float scale2,
+                                              float slope2,
                                               float cap_in, float cap_out, float &m_used, float &l, float &alpha,
                                               bool &rescale) {
   const float kNegInf = -CUDART_INF_F;
-  const float jf = (float)n0;
+  const float jf = (float)(n0 + kv_offset);
   // An opaque per-block copy of the slope keeps the compiler from hoisting
   // 128 per-column products slope * c out of the block loop into registers.
   float sl = slope2;
@@ -380,7 +381,7 @@ __device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
   const int r = threadIdx.x % kBM;
   const int row0 = m0 + t * kBM;
   const int qi = row0 + r;
-  const int off = kl - ql;
+  const int off = diag_shift(a, ql, kl);
   const int diag = qi + off;
   const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
   const uint32_t tS = tmem + lane_off + (t ? C::kTmemS1 : C::kTmemS0);
@@ -414,10 +415,10 @@ __device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
     float alpha = 1.f;
     bool rescale = false;
     if (need_mask)
-      softmax_block<T, kAlibi, kSoftcap, true>(tS, n0, lo, hi, scale2, slope2, cap_in, cap_out, m_used, l, alpha,
+      softmax_block<T, kAlibi, kSoftcap, true>(tS, n0, a.kv_offset, lo, hi, scale2, slope2, cap_in, cap_out, m_used, l, alpha,
                                                rescale);
     else
-      softmax_block<T, kAlibi, kSoftcap, false>(tS, n0, lo, hi, scale2, slope2, cap_in, cap_out, m_used, l, alpha,
+      softmax_block<T, kAlibi, kSoftcap, false>(tS, n0, a.kv_offset, lo, hi, scale2, slope2, cap_in, cap_out, m_used, l, alpha,
                                                 rescale);
     if (__any_sync(0xffffffffu, rescale)) {
       // O_t holds blocks 0..j-1 once PV_t(j-1) is done; rescale it in place.

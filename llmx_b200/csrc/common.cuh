@@ -93,10 +93,20 @@ __device__ __forceinline__ float score_transform(float dot, float sm_scale, floa
   return s + slope * (float)j;
 }
 
-// Visibility of key j to query row i (both sequence-local), mask.h:41-81.
-__device__ __forceinline__ bool key_visible(int i, int j, int ql, int kl, int causal, int window) {
+// Diagonal shift in local key indices: local key j is visible to query row i
+// under the causal rule when j <= i + doff (mask.h:54-63), where
+// doff = kfull - q_len - kv_offset and kfull is the full key length of the
+// sequence (kv_total, or the local length when the keys are not sharded).
+__device__ __forceinline__ int diag_shift(const AttnArgs &a, int ql, int kl) {
+  const int kfull = a.kv_total > 0 ? a.kv_total : kl;
+  return kfull - ql - a.kv_offset;
+}
+
+// Visibility of local key j to query row i, mask.h:41-81: inside the local
+// length, on or below the (shifted) diagonal, inside the window.
+__device__ __forceinline__ bool key_visible(int i, int j, int kl, int doff, int causal, int window) {
   if (j >= kl || j < 0) return false;
-  const int diag = i + (kl - ql);
+  const int diag = i + doff;
   if (causal && j > diag) return false;
   if (window >= 0 && (diag - j) > window) return false;
   return true;

@@ -1,6 +1,6 @@
 // Thin inline-PTX wrappers for the sm_100a features the prefill kernel uses:
-// mbarriers (every wait bounded in time), TMA tile loads (no cluster
-// multicast anywhere), tensor-memory allocation, tcgen05.mma / commit /
+// mbarriers (every wait bounded in time), TMA tile loads into this CTA's own
+// shared memory only, tensor-memory allocation, tcgen05.mma / commit /
 // ld / st, and the shared-memory matrix descriptors.
 //
 // Descriptor and instruction-descriptor bit layouts follow the PTX ISA's
@@ -172,6 +172,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
       "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
       : LLMX_R32(v)
       : "r"(taddr));
+}
+// 16 consecutive 32-bit columns of this warp's 32 lanes (see tmem_ld32).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void reg_fence16(uint32_t (&v)[16]) {
+  asm volatile("" : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]),
+               "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]),
+               "+r"(v[14]), "+r"(v[15]));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 

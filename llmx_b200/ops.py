@@ -11,8 +11,9 @@ device, n_heads divisible by n_kv_heads, matching head_dim), raising
 RuntimeError where the reference raises through TORCH_CHECK.  It adds the
 extended request as keyword arguments: ``alibi_slopes`` (the reference
 binding always passes nullopt, llmx_bind.cpp:69-71), ``causal``, ``q_lens``
-/ ``kv_lens`` (padding), ``lse``, 4-D [B, S, H, D] tensors, fp32, and it runs
-on torch's current stream instead of stream 0.
+/ ``kv_lens`` (padding), ``lse``, ``kv_offset`` / ``kv_total`` (key shards),
+4-D [B, S, H, D] tensors, fp32, and it runs on torch's current stream
+instead of stream 0.
 """
 
 from __future__ import annotations
@@ -52,6 +53,8 @@ def build_params(
     kv_lens: Optional[torch.Tensor] = None,
     lse: Optional[torch.Tensor] = None,
     algo: str = "auto",
+    kv_offset: int = 0,
+    kv_total: int = 0,
 ):
     """Validates torch tensors and returns (AttnParams, tensors to keep alive)."""
     nd = q.dim()
@@ -110,6 +113,7 @@ def build_params(
         _req(lse.device == q.device, "lse must be on q's device")
         p.lse = lse.data_ptr()
     p.sm_scale = float(sm_scale)
+    p.kv_offset, p.kv_total = int(kv_offset), int(kv_total)
     p.causal = 1 if causal else 0
     p.sliding_window = int(sliding_window)
     p.logits_soft_cap = float(logits_soft_cap)
@@ -145,11 +149,17 @@ def single_mha_attention_half(
     kv_lens: Optional[torch.Tensor] = None,
     lse: Optional[torch.Tensor] = None,
     algo: str = "auto",
+    kv_offset: int = 0,
+    kv_total: int = 0,
 ) -> None:
-    """Writes attention(q, k, v) into ``output`` (see the module docstring)."""
+    """Writes attention(q, k, v) into ``output`` (see the module docstring).
+
+    ``kv_offset`` / ``kv_total`` describe a shard of a sequence's keys: local
+    key j sits at global position kv_offset + j and the causal / window
+    diagonal uses the full key length kv_total (0: the local length)."""
     p, keep = build_params(output, q, k, v, sm_scale, sliding_window, logits_soft_cap,
                            alibi_slopes=alibi_slopes, causal=causal, q_lens=q_lens, kv_lens=kv_lens,
-                           lse=lse, algo=algo)
+                           lse=lse, algo=algo, kv_offset=kv_offset, kv_total=kv_total)
     _run(p, q.device, keep)
 
 

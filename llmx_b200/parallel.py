@@ -1,0 +1,160 @@
+"""Multi-GPU partitioning of the attention forward (one process per GPU).
+
+Two ways the work splits across GPUs of one node:
+
+* **batch x head shards** (independent units, no communication): every
+  (batch, head) pair is an independent attention problem.  ``shard_units``
+  gives each rank a contiguous, balanced slice of the flattened units; each
+  rank runs the kernel on its slice.
+* **KV split** for long sequences: each rank holds the full query block and a
+  share of the keys, computes (O_r, lse_r) over its keys with the kernel
+  (``kv_offset`` / ``kv_total`` place the shard's keys at their global
+  positions for the causal diagonal and ALiBi), and the partials are merged
+  exactly with the log-sum-exp rule
+
+      lse = log sum_r exp(lse_r),   O = sum_r exp(lse_r - lse) O_r
+
+  as NCCL all-reduce MAX of lse_r, a local rescale, and one all-reduce SUM of
+  [O_r * w_r | w_r] (w_r = exp(lse_r - max)).  For causal masking the keys
+  are dealt in zig-zag chunks (with 2n chunks, rank g takes chunks g and
+  2n-1-g) so that every rank gets the same amount of visible work.
+
+The reference has no multi-GPU code; its kernel already streams keys through
+an online softmax inside one SM (single_mha_kernel.cuh:294-340), and the
+merge here is the same running-max / running-sum algebra applied across
+shards instead of across blocks (softmax.h:53-110).
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from . import ops
+
+
+def shard_units(batch: int, heads: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous range [start, end) of flattened (batch, head) units for `rank`.
+
+    Unit u is (u // heads, u % heads); the ranges differ in size by at most
+    one unit and cover every unit exactly once.
+    """
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    units = batch * heads
+    base, extra = divmod(units, world)
+    start = rank * base + min(rank, extra)
+    end = start + base + (1 if rank < extra else 0)
+    return start, end
+
+
+def zigzag_chunks(seq_len: int, world: int, rank: int, align: int = 128) -> List[Tuple[int, int]]:
+    """Key ranges [start, end) of `rank` when `seq_len` keys are dealt in
+    2 * world chunks, rank g taking chunks g and 2 * world - 1 - g.
+
+    Chunk boundaries are multiples of `align` (the kernel's key block) except
+    the last; empty chunks are dropped.
+    """
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    n = 2 * world
+    step = -(-seq_len // n)
+    step = -(-step // align) * align
+    bounds = [min(seq_len, c * step) for c in range(n + 1)]
+    out = []
+    for c in sorted({rank, n - 1 - rank}):
+        if bounds[c + 1] > bounds[c]:
+            out.append((bounds[c], bounds[c + 1]))
+    return out
+
+
+def merge_partials(outs: Sequence[torch.Tensor], lses: Sequence[torch.Tensor]):
+    """Exact merge of attention partials over disjoint key sets (one rank).
+
+    outs: [B, S, H, D] each (any float type); lses: [B, H, S] fp32 natural-log
+    (-inf where a row saw no key).  Returns (O fp32 [B, S, H, D], lse [B, H, S]).
+    """
+    lse = torch.stack(list(lses), 0)  # [n, B, H, S]
+    m = lse.amax(0)
+    m_safe = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+    w = torch.exp(lse - m_safe)  # exp(-inf) = 0 for empty partials
+    wsum = w.sum(0)
+    num = None
+    for o, wi in zip(outs, w):
+        term = o.float() * wi.permute(0, 2, 1).unsqueeze(-1)
+        num = term if num is None else num + term
+    inv = torch.where(wsum > 0, 1.0 / wsum, torch.zeros_like(wsum))
+    out = num * inv.permute(0, 2, 1).unsqueeze(-1)
+    lse_out = torch.where(wsum > 0, m_safe + torch.log(wsum), torch.full_like(m, float("-inf")))
+    return out, lse_out
+
+
+def merge_across_ranks(out: torch.Tensor, lse: torch.Tensor, group=None):
+    """Exact merge of this rank's partial (out fp32 [B, S, H, D], lse [B, H, S])
+    with every other rank's, via all-reduce MAX then one all-reduce SUM.
+
+    Every rank returns the merged (O fp32, lse).  Works on any backend
+    torch.distributed supports for these ops (NCCL on GPUs, gloo on CPU).
+    """
+    import torch.distributed as dist
+
+    m = lse.clone()
+    dist.all_reduce(m, op=dist.ReduceOp.MAX, group=group)
+    m_safe = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+    w = torch.exp(lse - m_safe)  # [B, H, S]; 0 where this rank saw no key
+    B, S, H, D = out.shape
+    payload = torch.empty(B * S * H * D + B * H * S, dtype=torch.float32, device=out.device)
+    num = payload[: B * S * H * D].view(B, S, H, D)
+    torch.mul(out.float(), w.permute(0, 2, 1).unsqueeze(-1), out=num)
+    payload[B * S * H * D :].copy_(w.reshape(-1))
+    dist.all_reduce(payload, op=dist.ReduceOp.SUM, group=group)
+    wsum = payload[B * S * H * D :].view(B, H, S)
+    inv = torch.where(wsum > 0, 1.0 / wsum, torch.zeros_like(wsum))
+    merged = num * inv.permute(0, 2, 1).unsqueeze(-1)
+    lse_out = torch.where(wsum > 0, m_safe + torch.log(wsum), torch.full_like(m, float("-inf")))
+    return merged, lse_out
+
+
+def kv_split_attention(
+    q: torch.Tensor,
+    k_chunks: Sequence[torch.Tensor],
+    v_chunks: Sequence[torch.Tensor],
+    chunk_offsets: Sequence[int],
+    kv_total: int,
+    sm_scale: float,
+    *,
+    alibi_slopes: Optional[torch.Tensor] = None,
+    causal: bool = True,
+    sliding_window: int = -1,
+    group=None,
+    out_dtype: Optional[torch.dtype] = None,
+):
+    """Attention of all of `q` ([B, S, H, D]) over the keys of every rank,
+    where this rank holds the key chunks `k_chunks` / `v_chunks`
+    ([B, n_c, H_kv, D]) starting at global positions `chunk_offsets`.
+
+    Runs the kernel once per local chunk, merges the chunks locally and then
+    across the ranks of `group` (skipped when torch.distributed is not
+    initialised or the group has one rank).  Returns (O in `out_dtype`
+    (default q's), lse fp32 [B, H, S]) on every rank.
+    """
+    import torch.distributed as dist
+
+    B, S, H, D = q.shape
+    outs, lses = [], []
+    for kc, vc, off in zip(k_chunks, v_chunks, chunk_offsets):
+        o = torch.empty_like(q)
+        l = torch.empty(B, H, S, dtype=torch.float32, device=q.device)
+        ops.single_mha_attention_half(o, q, kc, vc, sm_scale, sliding_window, alibi_slopes=alibi_slopes,
+                                      causal=causal, lse=l, kv_offset=int(off), kv_total=int(kv_total))
+        outs.append(o)
+        lses.append(l)
+    if outs:
+        out, lse = merge_partials(outs, lses)
+    else:
+        out = torch.zeros(B, S, H, D, dtype=torch.float32, device=q.device)
+        lse = torch.full((B, H, S), float("-inf"), device=q.device)
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        out, lse = merge_across_ranks(out, lse, group)
+    return out.to(out_dtype or q.dtype), lse

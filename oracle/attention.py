@@ -28,8 +28,10 @@ against:
 Extensions beyond the reference signature (the same arithmetic, applied to
 more inputs): a ``causal=False`` mode, per-sequence query/key lengths for
 padded batches, a caller-supplied ``sm_scale`` (the kernel API takes one,
-``attention_api.h:8-14``; the reference oracle hard-codes 1/sqrt(D)), and the
-per-row log-sum-exp used by split-KV merging.  A row that sees no key at all
+``attention_api.h:8-14``; the reference oracle hard-codes 1/sqrt(D)), the
+per-row log-sum-exp used by split-KV merging, and key slices (``kv_offset``
+/ ``kv_total``: the same mask and ALiBi evaluated at the keys' global
+positions).  A row that sees no key at all
 (an empty sequence, or causal with kv_len < q_len) yields O = 0 and
 lse = -inf; the reference never produces such a row (it asserts
 kv_len >= q_len, test_attention.py:51).
@@ -55,15 +57,19 @@ def alibi_slopes(n_heads: int) -> torch.Tensor:
     return torch.pow(2.0, -8.0 * (h + 1.0) / n_heads).to(torch.float32)
 
 
-def _visible_mask(q_len: int, kv_len: int, causal: bool, sliding_window: int) -> torch.Tensor:
+def _visible_mask(q_len: int, kv_len: int, causal: bool, sliding_window: int, kv_offset: int = 0,
+                  kv_total: Optional[int] = None) -> torch.Tensor:
     """Boolean [q_len, kv_len] mask of the keys each query row may attend to.
 
     Bottom-right aligned causal mask and sliding window, restating
     ``mask.h:54-66`` / ``test_attention.py:79-85`` with explicit index compares.
+    For a slice of a sequence's keys, local key j sits at global position
+    kv_offset + j and the diagonal uses the full key length kv_total.
     """
+    kfull = kv_len if kv_total is None else kv_total
     i = torch.arange(q_len).view(q_len, 1)
-    j = torch.arange(kv_len).view(1, kv_len)
-    diag = i + (kv_len - q_len)  # query row i on the key axis
+    j = torch.arange(kv_len).view(1, kv_len) + kv_offset
+    diag = i + (kfull - q_len)  # query row i on the key axis
     vis = torch.ones(q_len, kv_len, dtype=torch.bool)
     if causal:
         vis &= j <= diag
@@ -84,6 +90,8 @@ def attention_ref(
     causal: bool = True,
     return_lse: bool = False,
     compute_dtype: torch.dtype = torch.float32,
+    kv_offset: int = 0,
+    kv_total: Optional[int] = None,
 ):
     """One sequence of attention on CPU.
 
@@ -112,10 +120,10 @@ def attention_ref(
     if logits_soft_cap != 0.0:
         s = torch.tanh(s / logits_soft_cap) * logits_soft_cap
     if alibi is not None:
-        j = torch.arange(kv_len, dtype=compute_dtype)
+        j = torch.arange(kv_len, dtype=compute_dtype) + kv_offset
         s = s + alibi.to(compute_dtype).view(n_heads, 1, 1) * j.view(1, 1, kv_len)
 
-    vis = _visible_mask(q_len, kv_len, causal, sliding_window)
+    vis = _visible_mask(q_len, kv_len, causal, sliding_window, kv_offset, kv_total)
     s = s.masked_fill(~vis.unsqueeze(0), float("-inf"))
 
     row_any = vis.any(dim=1)  # [q]

@@ -51,7 +51,7 @@ def test_struct_layout_matches_c():
 int main(void) {
   printf("size %zu\n", sizeof(llmx_attn_params));
   O(dtype) O(algo) O(q) O(o) O(q_stride) O(o_stride) O(q_lens) O(alibi_slopes) O(sm_scale)
-  O(causal) O(logits_soft_cap) O(lse) O(workspace) O(workspace_bytes)
+  O(causal) O(logits_soft_cap) O(lse) O(workspace) O(workspace_bytes) O(kv_offset) O(kv_total)
   return 0;
 }
 """
@@ -98,7 +98,7 @@ def test_defaults_and_contiguous_strides():
 @pytest.mark.parametrize("field,value", [
     ("dtype", 7), ("batch", 0), ("n_heads", 0), ("n_kv_heads", 3), ("head_dim", 0),
     ("head_dim", 257), ("max_q_len", 0), ("max_kv_len", 0), ("q", 0), ("algo", 9),
-    ("sm_scale", float("nan")),
+    ("sm_scale", float("nan")), ("kv_offset", -1), ("kv_total", -5),
 ])
 def test_invalid_arguments_rejected(field, value):
     lib = _lib.load()
@@ -141,4 +141,4 @@ def test_status_strings():
     lib = _lib.load()
     for code in _lib.STATUS_NAMES:
         assert lib.llmx_status_string(code)
-    assert lib.llmx_attn_abi_version() == 1
+    assert lib.llmx_attn_abi_version() == 2
