@@ -156,6 +156,26 @@ LLMX_API llmx_status llmx_single_mha_attention_c(void *output, const void *q, co
 #define LLMX_DECODE_NOALLOC_SCRATCH_BYTES (32u << 20)
 LLMX_API llmx_status llmx_attn_decode_noalloc(const llmx_attn_params *p, void *stream);
 
+/* Log-sum-exp merge of attention partials over disjoint key sets (keys
+ * split across calls or GPUs), in two steps around a cross-GPU SUM of
+ * [num | wsum].  No counterpart in the reference (it has no key splitting);
+ * the algebra is its online-softmax rescale (softmax.h:53-110) applied
+ * across shards.
+ *   outs[c]  : [batch, seq, n_heads, head_dim] partial O (fp16/bf16, contiguous)
+ *   lses[c]  : [batch, n_heads, seq] fp32 natural-log lse (-inf: no key seen)
+ *   row_max  : [batch, n_heads, seq] fp32 max of lse over every shard
+ *   num      : [batch, seq, n_heads, head_dim] fp32 = sum_c exp(lse_c - m) O_c
+ *   wsum     : [batch, n_heads, seq] fp32 = sum_c exp(lse_c - m)
+ * merge_finish writes out = num / wsum (0 where wsum == 0) in the partials'
+ * dtype and, if lse_out is not NULL, lse = m + log(wsum).  n_parts <= 8. */
+LLMX_API llmx_status llmx_attn_lse_merge_scale(int32_t n_parts, const void *const *outs, const float *const *lses,
+                                               const float *row_max, int32_t dtype, int32_t batch, int32_t seq,
+                                               int32_t n_heads, int32_t head_dim, float *num, float *wsum,
+                                               void *stream);
+LLMX_API llmx_status llmx_attn_lse_merge_finish(const float *num, const float *wsum, const float *row_max,
+                                                int32_t dtype, int32_t batch, int32_t seq, int32_t n_heads,
+                                                int32_t head_dim, void *out, float *lse_out, void *stream);
+
 /* Which kernel family llmx_attn_fwd would run for *p (an llmx_attn_algo). */
 LLMX_API llmx_status llmx_attn_select_algo(const llmx_attn_params *p, int32_t *algo);
 

@@ -77,6 +77,11 @@ SIGNATURES = {
     ),
     "llmx_attn_select_algo": (_i32, [ctypes.POINTER(AttnParams), ctypes.POINTER(_i32)]),
     "llmx_attn_decode_noalloc": (_i32, [ctypes.POINTER(AttnParams), _vp]),
+    "llmx_attn_lse_merge_scale": (
+        _i32,
+        [_i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp],
+    ),
+    "llmx_attn_lse_merge_finish": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
     "llmx_attn_device_status": (_i32, [_i32, _i32]),
     "llmx_status_string": (ctypes.c_char_p, [_i32]),
     "llmx_attn_last_error": (ctypes.c_char_p, []),

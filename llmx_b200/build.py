@@ -30,7 +30,7 @@ NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
 # Kernel and C-ABI units export only what include/llmx_attn.h marks LLMX_API;
 # the C++ Tensor / attention API units export their whole public surface.
 HIDDEN = ["-Xcompiler", "-fvisibility=hidden"]
-SOURCES = ["attn_api.cu", "attn_simt.cu", "attn_decode.cu", "attn_sm100.cu", "llmx_tensor.cu",
+SOURCES = ["attn_api.cu", "attn_simt.cu", "attn_decode.cu", "attn_sm100.cu", "attn_merge.cu", "llmx_tensor.cu",
            "attention_api.cu"]
 
 

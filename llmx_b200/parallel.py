@@ -134,10 +134,11 @@ def kv_split_attention(
     where this rank holds the key chunks `k_chunks` / `v_chunks`
     ([B, n_c, H_kv, D]) starting at global positions `chunk_offsets`.
 
-    Runs the kernel once per local chunk, merges the chunks locally and then
-    across the ranks of `group` (skipped when torch.distributed is not
-    initialised or the group has one rank).  Returns (O in `out_dtype`
-    (default q's), lse fp32 [B, H, S]) on every rank.
+    Runs the kernel once per local chunk and merges every chunk of every
+    rank of `group` exactly (cross-rank steps skipped when torch.distributed
+    is not initialised or the group has one rank) with the library's merge
+    kernels.  Returns (O in `out_dtype` (default q's), lse fp32 [B, H, S]) on
+    every rank.
     """
     import torch.distributed as dist
 
@@ -150,11 +151,50 @@ def kv_split_attention(
                                       causal=causal, lse=l, kv_offset=int(off), kv_total=int(kv_total))
         outs.append(o)
         lses.append(l)
-    if outs:
-        out, lse = merge_partials(outs, lses)
+    multi = dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
+    return _merge_cuda(outs, lses, q, multi, group, out_dtype)
+
+
+def _merge_cuda(outs, lses, q, multi, group, out_dtype):
+    """The merge on the GPU: row max of lse over every shard (all-reduce MAX),
+    one scale kernel writing [num | wsum] for the local partials, one
+    all-reduce SUM of that buffer, one finish kernel."""
+    import ctypes
+
+    import torch.distributed as dist
+
+    from . import _lib
+
+    B, S, H, D = q.shape
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError("the KV-split merge takes fp16 or bf16 partials")
+    if lses:
+        m = torch.stack(list(lses), 0).amax(0)
     else:
-        out = torch.zeros(B, S, H, D, dtype=torch.float32, device=q.device)
-        lse = torch.full((B, H, S), float("-inf"), device=q.device)
-    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
-        out, lse = merge_across_ranks(out, lse, group)
-    return out.to(out_dtype or q.dtype), lse
+        m = torch.full((B, H, S), float("-inf"), device=q.device)
+    if multi:
+        dist.all_reduce(m, op=dist.ReduceOp.MAX, group=group)
+    n = B * S * H * D
+    payload = torch.empty(n + B * H * S, dtype=torch.float32, device=q.device)
+    num, wsum = payload[:n], payload[n:]
+    lib = _lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)
+    dt = _lib.DTYPE["bf16" if q.dtype == torch.bfloat16 else "fp16"]
+    outs = [o.contiguous() for o in outs]
+    optrs = (ctypes.c_void_p * max(1, len(outs)))(*[o.data_ptr() for o in outs])
+    lptrs = (ctypes.c_void_p * max(1, len(lses)))(*[l.data_ptr() for l in lses])
+    _lib.check(lib.llmx_attn_lse_merge_scale(len(outs), optrs, lptrs, m.data_ptr(), dt, B, S, H, D,
+                                             num.data_ptr(), wsum.data_ptr(), stream))
+    if multi:
+        dist.all_reduce(payload, op=dist.ReduceOp.SUM, group=group)
+    out = torch.empty(B, S, H, D, dtype=out_dtype or q.dtype, device=q.device)
+    if out.dtype != q.dtype:
+        tmp = torch.empty_like(q)
+    else:
+        tmp = out
+    lse = torch.empty(B, H, S, dtype=torch.float32, device=q.device)
+    _lib.check(lib.llmx_attn_lse_merge_finish(num.data_ptr(), wsum.data_ptr(), m.data_ptr(), dt, B, S, H, D,
+                                              tmp.data_ptr(), lse.data_ptr(), stream))
+    if tmp is not out:
+        out.copy_(tmp)
+    return out, lse

@@ -102,3 +102,22 @@ def test_kv_split_two_gpus_nccl(tmp_path):
     llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, alibi_slopes=oracle.alibi_slopes(H).cuda())
     torch.cuda.synchronize()
     assert (res["out"].float() - full.float().cpu()).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("n_parts", [1, 2, 3, 8])
+def test_merge_kernels_match_torch_merge(n_parts):
+    B, S, H, D = 2, 96, 3, 64
+    g = torch.Generator().manual_seed(n_parts)
+    outs = [torch.randn(B, S, H, D, generator=g).to(torch.bfloat16).cuda() for _ in range(n_parts)]
+    lses = [torch.randn(B, H, S, generator=g).cuda() * 3 for _ in range(n_parts)]
+    lses[0][:, :, :5] = float("-inf")  # rows the first shard never saw
+    if n_parts == 1:
+        lses[0][0, 0, 7] = float("-inf")  # a row nobody saw
+    q = torch.empty(B, S, H, D, dtype=torch.bfloat16, device="cuda")
+    out, lse = parallel._merge_cuda(outs, lses, q, False, None, None)
+    ref, lref = parallel.merge_partials([o.cpu() for o in outs], [l.cpu() for l in lses])
+    torch.cuda.synchronize()
+    assert (out.float().cpu() - ref).abs().max().item() <= 2e-2
+    fin = torch.isfinite(lref)
+    assert torch.equal(torch.isfinite(lse.cpu()), fin)
+    torch.testing.assert_close(lse.cpu()[fin], lref[fin], atol=1e-4, rtol=0)
