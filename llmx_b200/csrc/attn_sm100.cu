@@ -84,7 +84,7 @@ struct Cfg {
 };
 
 struct Bars {
-  uint64_t q_full;
+  uint64_t q_full[2];  // one per query tile
   uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
   uint64_t s_full[2], p_full[2], o_done[2];
   uint64_t drain;
@@ -134,11 +134,13 @@ __device__ void tma_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k, const
                          uint8_t *smem, Bars *bars, unsigned int *err, int m0, int h, int kvh, int b,
                          BlockRange br) {
   using C = Cfg<D>;
-  mbar_arrive_expect_tx(&bars->q_full, kTiles * C::kTileBytes);
-  for (int t = 0; t < kTiles; ++t)
+  auto load_q = [&](int t) {
+    mbar_arrive_expect_tx(&bars->q_full[t], C::kTileBytes);
     for (int c = 0; c < C::kChunks; ++c)
-      tma_load_4d(smem + C::kQOff + t * C::kTileBytes + c * C::kChunkBytes, tm_q, &bars->q_full, c * 64, h,
+      tma_load_4d(smem + C::kQOff + t * C::kTileBytes + c * C::kChunkBytes, tm_q, &bars->q_full[t], c * 64, h,
                   m0 + t * kBM, b);
+  };
+  load_q(0);
   int issued_k = 0, issued_v = 0;
   for (int j = 0; j < br.nb; ++j) {
     const int s = j % C::kStages;
@@ -153,6 +155,7 @@ __device__ void tma_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k, const
       tma_load_4d(smem + C::kKOff + s * C::kTileBytes + c * C::kChunkBytes, tm_k, &bars->k_full[s], c * 64, kvh,
                   n0, b);
     issued_k = j + 1;
+    if (j == 0) load_q(1);
     if (!mbar_wait(&bars->v_empty[s], par, kTimeoutNs)) {
       set_abort(bars, err);
       break;
@@ -166,7 +169,8 @@ __device__ void tma_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k, const
   }
   // Drain: every load issued must have landed before the CTA may exit.  In a
   // normal run these phases completed long ago and the waits return at once.
-  mbar_wait(&bars->q_full, 0, kTimeoutNs);
+  mbar_wait(&bars->q_full[0], 0, kTimeoutNs);
+  if (issued_k > 0) mbar_wait(&bars->q_full[1], 0, kTimeoutNs);
   for (int j = max(0, issued_k - C::kStages); j < issued_k; ++j)
     mbar_wait(&bars->k_full[j % C::kStages], (j / C::kStages) & 1, kTimeoutNs);
   for (int j = max(0, issued_v - C::kStages); j < issued_v; ++j)
@@ -206,12 +210,16 @@ __device__ void mma_role(uint8_t *smem, Bars *bars, unsigned int *err, uint32_t 
     }
   };
 
-  bool ok = mbar_wait(&bars->q_full, 0, kTimeoutNs) && mbar_wait(&bars->k_full[0], 0, kTimeoutNs);
-  if (!ok) set_abort(bars, err);
+  bool ok = mbar_wait(&bars->q_full[0], 0, kTimeoutNs) && mbar_wait(&bars->k_full[0], 0, kTimeoutNs);
   if (ok) {
     tc_fence_after();
     issue_qk(0, 0);
     tc_commit(&bars->s_full[0]);
+    ok = mbar_wait(&bars->q_full[1], 0, kTimeoutNs);
+  }
+  if (!ok) set_abort(bars, err);
+  if (ok) {
+    tc_fence_after();
     issue_qk(1, 0);
     tc_commit(&bars->s_full[1]);
     tc_commit(&bars->k_empty[0]);
@@ -322,6 +330,79 @@ __device__ __forceinline__ float chunk_exp(const uint32_t (&v)[32], uint32_t (&p
   return (s[0] + s[1]) + (s[2] + s[3]);
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): two scores per instruction.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// ALiBi path with packed fp32 pairs: the bias slope * (jf + c) is carried
+// pairwise with one f32x2 add, and score * scale + bias (- m) is one f32x2
+// FMA per pair, halving the arithmetic the bias would otherwise add.
+template <bool kMask>
+__device__ __forceinline__ float chunk_max_alibi(const uint32_t (&v)[32], int c0, int lo, int hi, float scale2,
+                                                 float slope2, float jf) {
+  float m[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m[i] = -CUDART_INF_F;
+  const uint64_t sc = f2(scale2, scale2), step = f2(2.f * slope2, 2.f * slope2);
+  uint64_t bias = f2(slope2 * (jf + (float)c0), slope2 * (jf + (float)(c0 + 1)));
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    float y0, y1;
+    f2_split(fma2(f2(__uint_as_float(v[c]), __uint_as_float(v[c + 1])), sc, bias), y0, y1);
+    bias = add2(bias, step);
+    if (kMask) {
+      y0 = (c0 + c >= lo && c0 + c < hi) ? y0 : -CUDART_INF_F;
+      y1 = (c0 + c + 1 >= lo && c0 + c + 1 < hi) ? y1 : -CUDART_INF_F;
+    }
+    m[(c >> 1) & 3] = fmax3(m[(c >> 1) & 3], y0, y1);
+  }
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
+template <typename T, bool kMask>
+__device__ __forceinline__ float chunk_exp_alibi(const uint32_t (&v)[32], uint32_t (&pk)[16], int c0, int lo, int hi,
+                                                 float scale2, float slope2, float jf, float m) {
+  uint64_t acc0 = f2(0.f, 0.f), acc1 = f2(0.f, 0.f);
+  const uint64_t sc = f2(scale2, scale2), step = f2(2.f * slope2, 2.f * slope2);
+  uint64_t off = f2(slope2 * (jf + (float)c0) - m, slope2 * (jf + (float)(c0 + 1)) - m);
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    float y0, y1;
+    f2_split(fma2(f2(__uint_as_float(v[c]), __uint_as_float(v[c + 1])), sc, off), y0, y1);
+    off = add2(off, step);
+    if (kMask) {
+      y0 = (c0 + c >= lo && c0 + c < hi) ? y0 : -CUDART_INF_F;
+      y1 = (c0 + c + 1 >= lo && c0 + c + 1 < hi) ? y1 : -CUDART_INF_F;
+    }
+    const float p0 = ex2_approx(y0), p1 = ex2_approx(y1);
+    if ((c >> 1) & 1)
+      acc1 = add2(acc1, f2(p0, p1));
+    else
+      acc0 = add2(acc0, f2(p0, p1));
+    pk[c / 2] = pack2<T>(p0, p1);
+  }
+  float a, b, cc, d;
+  f2_split(acc0, a, b);
+  f2_split(acc1, cc, d);
+  return (a + b) + (cc + d);
+}
+
 // One KV block of one row: load S (128 columns, one TMEM round trip), row
 // max, the rescale decision, P = 2^(s - m) written back over S as 16-bit
 // pairs, and the running sum.  kMask selects the per-column interval test;
@@ -346,7 +427,10 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int kv_offset
   float mx = kNegInf;
 #pragma unroll
   for (int q = 0; q < 4; ++q)
-    mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, kMask>(sr[q], q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out));
+    if constexpr (kAlibi && !kSoftcap)
+      mx = fmaxf(mx, chunk_max_alibi<kMask>(sr[q], q * 32, lo, hi, scale2, sl, jf));
+    else
+      mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, kMask>(sr[q], q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out));
   // Fresh names for the raw scores: pass 2 recomputes each transformed
   // score instead of keeping pass 1's values alive next to the raw row.
 #pragma unroll
@@ -364,7 +448,10 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int kv_offset
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint32_t pk[16];
-    psum += chunk_exp<T, kAlibi, kSoftcap, kMask>(sr[q], pk, q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out, m_eff);
+    if constexpr (kAlibi && !kSoftcap)
+      psum += chunk_exp_alibi<T, kMask>(sr[q], pk, q * 32, lo, hi, scale2, sl, jf, m_eff);
+    else
+      psum += chunk_exp<T, kAlibi, kSoftcap, kMask>(sr[q], pk, q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out, m_eff);
     tmem_st16(tS + q * 16, pk);
   }
   l = l * alpha + psum;
@@ -518,7 +605,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const BlockRange br = block_range(a, m0, ql, kl);
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_full[0], 1);
+    mbar_init(&bars->q_full[1], 1);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);

@@ -1,0 +1,150 @@
+// C++ API checks, built without gtest (none is available offline) and run by
+// tests/test_cpp_api_gpu.py.  Mirrors the reference's C++ tests:
+//  * Tensor semantics of test/tensor_test.cpp: zero-filled allocation,
+//    metadata-only resize, no reallocation when shrinking, reallocation when
+//    growing, host <-> device round trip, shared ownership on copy;
+//  * the attention smoke run of test/cuda/mha_attention_test.cpp (h=4,
+//    kv_h=2, S=256, D=128, fp16, zero inputs), now with its output checked;
+//  * a known answer: with q = 0 every visible key gets the same weight, so
+//    causal O[i] is the mean of V[0..i] (per kv head), computed here on the host.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <stdexcept>
+#include <vector>
+
+#include "llmx/cuda/attention/attention_api.h"
+#include "llmx/tensor.h"
+
+using namespace llmx;
+
+static int g_fail = 0;
+#define EXPECT(cond)                                                   \
+  do {                                                                 \
+    if (!(cond)) {                                                     \
+      std::fprintf(stderr, "FAIL %s:%d: %s\n", __FILE__, __LINE__, #cond); \
+      ++g_fail;                                                        \
+    }                                                                  \
+  } while (0)
+
+static void tensor_semantics() {
+  Device cpu(DeviceType::kCPU), gpu(DeviceType::kCUDA, 0);
+  Tensor t({2, 3, 4}, ScalarType::kFP32, cpu);
+  EXPECT(t.numel() == 24 && t.capacity() == 24 && t.contiguous());
+  EXPECT(t.stride(0) == 12 && t.stride(1) == 4 && t.stride(2) == 1 && t.count(1) == 12);
+  const float *p = t.const_data_ptr<float>();
+  bool zero = true;
+  for (int i = 0; i < 24; ++i) zero = zero && p[i] == 0.f;
+  EXPECT(zero);
+  void *before = t.data_ptr();
+  t.resize({4, 3});  // metadata only
+  EXPECT(t.data_ptr() == before && t.numel() == 12 && t.capacity() == 24);
+  t.allocate();  // shrinking: keeps the storage
+  EXPECT(t.data_ptr() == before);
+  t.resize({8, 8});
+  t.allocate();  // growing: new storage
+  EXPECT(t.capacity() == 64);
+  for (int i = 0; i < 64; ++i) t.data_ptr<float>()[i] = float(i);
+  t.to_device(gpu);
+  EXPECT(t.device() == gpu);
+  t.to_device(cpu);
+  bool same = true;
+  for (int i = 0; i < 64; ++i) same = same && t.const_data_ptr<float>()[i] == float(i);
+  EXPECT(same);
+  Tensor u = t;  // shares storage
+  EXPECT(u.data_ptr() == t.data_ptr() && t.data().use_count() == 2);
+}
+
+template <typename T>
+static std::vector<float> to_float(const std::vector<T> &v) {
+  std::vector<float> f(v.size());
+  for (size_t i = 0; i < v.size(); ++i) {
+    if constexpr (std::is_same<T, __half>::value)
+      f[i] = __half2float(v[i]);
+    else
+      f[i] = __bfloat162float(v[i]);
+  }
+  return f;
+}
+
+static void smoke_zero_inputs() {
+  // test/cuda/mha_attention_test.cpp: all-zero q/k/v, causal, no ALiBi.
+  const int S = 256, H = 4, Hkv = 2, D = 128;
+  Device gpu(DeviceType::kCUDA, 0);
+  Tensor q({S, H, D}, ScalarType::kFP16, gpu), k({S, Hkv, D}, ScalarType::kFP16, gpu),
+      v({S, Hkv, D}, ScalarType::kFP16, gpu), o({S, H, D}, ScalarType::kFP16, gpu);
+  llmx_single_mha_attention(o, q, k, v, std::nullopt, 1.0f / std::sqrt(float(D)));
+  EXPECT(cudaDeviceSynchronize() == cudaSuccess);
+  std::vector<__half> h(o.numel());
+  llmx_copy(gpu, Device(DeviceType::kCPU), o.const_data_ptr(), h.data(), o.nbytes());
+  bool zero = true;
+  for (auto x : to_float(h)) zero = zero && x == 0.f;
+  EXPECT(zero);
+}
+
+static void known_answer_uniform_weights() {
+  const int S = 200, H = 4, Hkv = 2, D = 64;
+  Device gpu(DeviceType::kCUDA, 0), cpu(DeviceType::kCPU);
+  std::vector<__nv_bfloat16> hq(S * H * D, __float2bfloat16(0.f)), hk(S * Hkv * D), hv(S * Hkv * D);
+  unsigned s = 12345u;
+  auto rnd = [&] {
+    s = s * 1664525u + 1013904223u;
+    return float((s >> 8) & 0xffff) / 65536.f - 0.5f;
+  };
+  for (auto &x : hk) x = __float2bfloat16(rnd());
+  for (auto &x : hv) x = __float2bfloat16(rnd());
+  Tensor q({S, H, D}, ScalarType::kBF16, gpu), k({S, Hkv, D}, ScalarType::kBF16, gpu),
+      v({S, Hkv, D}, ScalarType::kBF16, gpu), o({S, H, D}, ScalarType::kBF16, gpu);
+  llmx_copy(cpu, gpu, hq.data(), q.data_ptr(), q.nbytes());
+  llmx_copy(cpu, gpu, hk.data(), k.data_ptr(), k.nbytes());
+  llmx_copy(cpu, gpu, hv.data(), v.data_ptr(), v.nbytes());
+  llmx_single_mha_attention(o, q, k, v, std::nullopt, 0.125f);
+  EXPECT(cudaDeviceSynchronize() == cudaSuccess);
+  std::vector<__nv_bfloat16> ho(o.numel());
+  llmx_copy(gpu, cpu, o.const_data_ptr(), ho.data(), o.nbytes());
+  const std::vector<float> fo = to_float(ho), fv = to_float(hv);
+  double max_err = 0;
+  for (int h = 0; h < H; ++h) {
+    const int kvh = h / (H / Hkv);
+    for (int d = 0; d < D; ++d) {
+      double run = 0;
+      for (int i = 0; i < S; ++i) {
+        run += fv[(i * Hkv + kvh) * D + d];
+        const double want = run / (i + 1);
+        max_err = std::fmax(max_err, std::fabs(want - fo[(i * H + h) * D + d]));
+      }
+    }
+  }
+  std::printf("known answer max error %.3e\n", max_err);
+  EXPECT(max_err < 1e-2);
+}
+
+static void argument_errors_throw() {
+  Device gpu(DeviceType::kCUDA, 0);
+  Tensor q({16, 4, 64}, ScalarType::kFP16, gpu), k({16, 3, 64}, ScalarType::kFP16, gpu),
+      v({16, 3, 64}, ScalarType::kFP16, gpu), o({16, 4, 64}, ScalarType::kFP16, gpu);
+  bool threw = false;
+  try {
+    llmx_single_mha_attention(o, q, k, v, std::nullopt, 0.125f);  // 4 heads over 3 kv heads
+  } catch (const std::runtime_error &) {
+    threw = true;
+  }
+  EXPECT(threw);
+}
+
+int main() {
+  tensor_semantics();
+  smoke_zero_inputs();
+  known_answer_uniform_weights();
+  argument_errors_throw();
+  if (g_fail) {
+    std::fprintf(stderr, "%d check(s) failed\n", g_fail);
+    return 1;
+  }
+  std::printf("all C++ API checks passed\n");
+  return 0;
+}
