@@ -40,6 +40,11 @@ struct Device {
 void *llmx_allocate(size_t nbytes, Device device);
 void llmx_free(void *data, Device device);
 void llmx_copy(Device src_device, Device dst_device, const void *src, void *dst, size_t nbytes);
+// Element-type conversion of `num` contiguous elements in device-addressable
+// memory (src/tensor.cpp:108-118), on the legacy stream like the reference's
+// scalar_convert_kernel launch.  Same types copy.  Throws std::runtime_error
+// on a failing or refused launch (pageable host pointers are refused).
+void llmx_copy(ScalarType src_dtype, ScalarType dst_dtype, const void *src, void *dst, size_t num);
 
 // Pointer plus (for storage the allocator made) a shared owner.
 class DataPtr {
@@ -91,7 +96,9 @@ class Tensor {
 
   bool is_valid() const noexcept { return data_.ptr() != nullptr && capacity_ > 0; }
   bool contiguous() const noexcept;
-  size_t nbytes() const noexcept { return capacity_ * get_scalar_size(dtype_); }
+  // Bytes of storage held.  Tracked in bytes, so a tensor whose dtype was
+  // changed to a wider type reallocates on allocate() even at equal numel.
+  size_t nbytes() const noexcept { return storage_bytes_; }
   size_t capacity() const noexcept { return capacity_; }
   size_t count(int axis = 0) const noexcept { return size_t(dims_[axis]) * strides_[axis]; }
   size_t numel() const noexcept {
@@ -113,6 +120,7 @@ class Tensor {
   std::vector<int> dims_;
   std::vector<int> strides_;
   size_t capacity_ = 0;
+  size_t storage_bytes_ = 0;
   Device device_ = Device(DeviceType::kCPU);
 };
 

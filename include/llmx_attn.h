@@ -176,6 +176,19 @@ LLMX_API llmx_status llmx_attn_lse_merge_finish(const float *num, const float *w
                                                 int32_t dtype, int32_t batch, int32_t seq, int32_t n_heads,
                                                 int32_t head_dim, void *out, float *lse_out, void *stream);
 
+/* Element-type conversion of n contiguous elements between fp32, fp16 and
+ * bf16 (round to nearest even), enqueued on `stream`.  Replaces the
+ * reference's llmx_copy(ScalarType, ScalarType, ...) (src/tensor.cpp:108-118)
+ * and the launch_scalar_convert kernels behind it (src/scalar.cu:33-62),
+ * which back the to_fp32 / to_fp16 / to_bf16 ops (include/llmx/ops.h:25-74,
+ * 215-229).  fp16 <-> bf16 goes through fp32 as in scalar.cu:6-31.  When the
+ * two types match the elements are copied (the reference's same-type
+ * converter leaves the output unwritten, include/llmx/scalar.h:13-15).
+ * Any pointer alignment is accepted; 16-byte aligned buffers take the
+ * vector path. */
+LLMX_API llmx_status llmx_convert(const void *src, int32_t src_dtype, void *dst, int32_t dst_dtype, size_t n,
+                                  void *stream);
+
 /* Which kernel family llmx_attn_fwd would run for *p (an llmx_attn_algo). */
 LLMX_API llmx_status llmx_attn_select_algo(const llmx_attn_params *p, int32_t *algo);
 

@@ -6,6 +6,7 @@ use and every op raises if it has not been built -- there is no fallback
 path.  Build it with `python -m llmx_b200.build`.
 """
 from ._lib import LlmxError, load  # noqa: F401
-from .ops import attention, device_status, selected_algo, single_mha_attention_half  # noqa: F401
+from .ops import attention, convert, device_status, selected_algo, single_mha_attention_half  # noqa: F401
 
-__all__ = ["single_mha_attention_half", "attention", "selected_algo", "device_status", "LlmxError", "load"]
+__all__ = ["single_mha_attention_half", "attention", "convert", "selected_algo", "device_status", "LlmxError",
+           "load"]

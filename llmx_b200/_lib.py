@@ -82,6 +82,7 @@ SIGNATURES = {
         [_i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp],
     ),
     "llmx_attn_lse_merge_finish": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
+    "llmx_convert": (_i32, [_vp, _i32, _vp, _i32, ctypes.c_size_t, _vp]),
     "llmx_attn_device_status": (_i32, [_i32, _i32]),
     "llmx_status_string": (ctypes.c_char_p, [_i32]),
     "llmx_attn_last_error": (ctypes.c_char_p, []),

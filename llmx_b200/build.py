@@ -30,8 +30,10 @@ NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
 # Kernel and C-ABI units export only what include/llmx_attn.h marks LLMX_API;
 # the C++ Tensor / attention API units export their whole public surface.
 HIDDEN = ["-Xcompiler", "-fvisibility=hidden"]
-SOURCES = ["attn_api.cu", "attn_simt.cu", "attn_decode.cu", "attn_sm100.cu", "attn_merge.cu", "llmx_tensor.cu",
-           "attention_api.cu"]
+SOURCES = ["attn_api.cu", "attn_simt.cu", "attn_decode.cu", "attn_sm100.cu", "attn_merge.cu", "llmx_convert.cu",
+           "llmx_tensor.cu", "attention_api.cu", "llmx_ops.cu"]
+# The C++ Tensor / attention / registry units; every other unit is compiled hidden.
+CXX_API_UNITS = ("llmx_tensor.cu", "attention_api.cu", "llmx_ops.cu")
 
 
 def nvcc() -> str:
@@ -55,7 +57,7 @@ def _stale(obj: str, src: str, headers) -> bool:
 
 
 def _compile(src: str, obj: str, extra) -> str:
-    vis = HIDDEN if os.path.basename(src).startswith("attn_") else []
+    vis = [] if os.path.basename(src) in CXX_API_UNITS else HIDDEN
     cmd = [nvcc(), *NVCC_FLAGS, *vis, *extra, "-c", src, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:

@@ -31,6 +31,15 @@ void check(bool ok, const char *msg) {
   if (!ok) throw std::runtime_error(std::string("llmx attention: ") + msg);
 }
 
+bool on_cuda(const Tensor &t) { return t.device().type == DeviceType::kCUDA; }
+
+void check_devices(const Tensor &output, const Tensor &q, const Tensor &k, const Tensor &v,
+                   const std::optional<Tensor> &alibi_slopes) {
+  check(on_cuda(output) && on_cuda(q) && on_cuda(k) && on_cuda(v) &&
+            (!alibi_slopes.has_value() || on_cuda(*alibi_slopes)),
+        "tensors (and alibi_slopes) must be CUDA tensors");
+}
+
 void check_status(llmx_status s) {
   if (s != LLMX_OK)
     throw std::runtime_error(std::string("llmx attention: ") + llmx_status_string(s) + ": " +
@@ -69,6 +78,7 @@ void llmx_single_mha_attention(Tensor &output, const Tensor &q, const Tensor &k,
         "tensors must be contiguous");
   check(q.ndim() == 3 && k.ndim() == 3 && v.ndim() == 3 && output.ndim() == 3,
         "q, k, v, output must be 3-D [seq, heads, head_dim]");
+  check_devices(output, q, k, v, alibi_slopes);
   check(q.dtype() == k.dtype() && q.dtype() == v.dtype() && q.dtype() == output.dtype(),
         "q, k, v, output must share a dtype");
   if (alibi_slopes.has_value())
@@ -89,6 +99,7 @@ void llmx_mha_attention(Tensor &output, const Tensor &q, const Tensor &k, const 
   check((three && k.ndim() == 3 && v.ndim() == 3 && output.ndim() == 3) ||
             (q.ndim() == 4 && k.ndim() == 4 && v.ndim() == 4 && output.ndim() == 4),
         "tensors must all be 3-D [S, H, D] or all 4-D [B, S, H, D]");
+  check_devices(output, q, k, v, alibi_slopes);
   const int o = three ? 1 : 0;
   llmx_attn_params p;
   llmx_attn_params_init(&p);
@@ -104,6 +115,9 @@ void llmx_mha_attention(Tensor &output, const Tensor &q, const Tensor &k, const 
   p.v = v.const_data_ptr();
   p.o = output.data_ptr();
   llmx_attn_set_contiguous_strides(&p);
+  if (alibi_slopes.has_value())
+    check(alibi_slopes->dtype() == ScalarType::kFP32 && alibi_slopes->numel() == size_t(p.n_heads),
+          "alibi_slopes must be fp32 [n_heads]");
   p.alibi_slopes = alibi_slopes.has_value() ? alibi_slopes->const_data_ptr<float>() : nullptr;
   p.sm_scale = sm_scale;
   p.causal = opts.causal ? 1 : 0;

@@ -10,6 +10,7 @@
 #include <string>
 
 #include "llmx/tensor.h"
+#include "llmx_attn.h"
 
 namespace llmx {
 namespace {
@@ -66,6 +67,14 @@ void llmx_copy(Device src_device, Device dst_device, const void *src, void *dst,
   cuda_ok(cudaMemcpy(dst, src, nbytes, cudaMemcpyDefault), "cudaMemcpy");
 }
 
+void llmx_copy(ScalarType src_dtype, ScalarType dst_dtype, const void *src, void *dst, size_t num) {
+  if (num == 0) return;
+  if (src == nullptr || dst == nullptr) throw std::invalid_argument("llmx_copy: null pointer");
+  const llmx_status s = llmx_convert(src, static_cast<int32_t>(src_dtype), dst, static_cast<int32_t>(dst_dtype), num,
+                                     nullptr);
+  if (s != LLMX_OK) throw std::runtime_error(std::string("llmx_copy: ") + llmx_attn_last_error());
+}
+
 DataPtr::DataPtr(void *ptr, Device device)
     : ptr_(ptr), owner_(ptr, [device](void *p) { llmx_free(p, device); }) {}
 
@@ -79,6 +88,7 @@ Tensor::Tensor(void *data, const std::vector<int> &dims, ScalarType dtype, Devic
     : data_(data), dtype_(dtype), device_(device) {
   set_dims(dims);
   capacity_ = numel();
+  storage_bytes_ = capacity_ * get_scalar_size(dtype_);
 }
 
 void Tensor::set_dims(const std::vector<int> &dims) {
@@ -97,10 +107,12 @@ bool Tensor::contiguous() const noexcept {
 
 void Tensor::allocate() {
   const size_t n = numel();
-  if (data_.ptr() != nullptr && n <= capacity_) return;
-  void *p = llmx_allocate(n * get_scalar_size(dtype_), device_);
+  const size_t need = n * get_scalar_size(dtype_);
+  if (data_.ptr() != nullptr && need <= storage_bytes_) return;
+  void *p = llmx_allocate(need, device_);
   data_ = DataPtr(p, device_);
   capacity_ = n;
+  storage_bytes_ = need;
 }
 
 void Tensor::resize(const std::vector<int> &dims) { set_dims(dims); }
@@ -111,8 +123,8 @@ void Tensor::to_device(Device device, bool transfer) {
     device_ = device;
     return;
   }
-  void *p = llmx_allocate(capacity_ * get_scalar_size(dtype_), device);
-  if (transfer) llmx_copy(device_, device, data_.ptr(), p, capacity_ * get_scalar_size(dtype_));
+  void *p = llmx_allocate(storage_bytes_, device);
+  if (transfer) llmx_copy(device_, device, data_.ptr(), p, storage_bytes_);
   data_ = DataPtr(p, device);
   device_ = device;
 }

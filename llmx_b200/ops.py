@@ -183,3 +183,24 @@ def selected_algo(output, q, k, v, sm_scale, **kw) -> str:
 def device_status(device: int = 0, clear: bool = True) -> None:
     """Raises LlmxError if a kernel on `device` gave up on a bounded wait."""
     _lib.check(_lib.load().llmx_attn_device_status(int(device), 1 if clear else 0))
+
+
+def convert(x: torch.Tensor, dtype: torch.dtype, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Element-type conversion between fp32, fp16 and bf16 on the library's
+    kernel (the to_fp32 / to_fp16 / to_bf16 ops, include/llmx/ops.h:25-74 and
+    src/scalar.cu:33-46 in the reference), round to nearest even, on torch's
+    current stream.  ``x`` is a contiguous CUDA tensor; ``out`` (optional) a
+    contiguous CUDA tensor of ``dtype`` with as many elements."""
+    _req(x.is_cuda, "convert: input must be a CUDA tensor")
+    _req(x.dtype in _TORCH_DTYPE and dtype in _TORCH_DTYPE, "convert: dtypes must be fp32, fp16 or bf16")
+    _req(x.is_contiguous(), "convert: input must be contiguous")
+    if out is None:
+        out = torch.empty(x.shape, dtype=dtype, device=x.device)
+    _req(out.is_cuda and out.device == x.device and out.dtype == dtype and out.is_contiguous()
+         and out.numel() == x.numel(), "convert: out must be a contiguous CUDA tensor of dtype with x's size")
+    with torch.cuda.device(x.device):
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.check(_lib.load().llmx_convert(ctypes.c_void_p(x.data_ptr()), _lib.DTYPE[_TORCH_DTYPE[x.dtype]],
+                                            ctypes.c_void_p(out.data_ptr()), _lib.DTYPE[_TORCH_DTYPE[dtype]],
+                                            x.numel(), ctypes.c_void_p(stream)))
+    return out

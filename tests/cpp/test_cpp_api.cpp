@@ -6,7 +6,12 @@
 //  * the attention smoke run of test/cuda/mha_attention_test.cpp (h=4,
 //    kv_h=2, S=256, D=128, fp16, zero inputs), now with its output checked;
 //  * a known answer: with q = 0 every visible key gets the same weight, so
-//    causal O[i] is the mean of V[0..i] (per kv head), computed here on the host.
+//    causal O[i] is the mean of V[0..i] (per kv head), computed here on the host;
+//  * the operator registry (include/llmx/ops.h): test/ops_test.cpp:8-31's
+//    fp16 [1, 2, 3, 4] -> to_fp32 known answer, to_fp16 / to_bf16 (the
+//    reference's to_fp16 cannot run: it looks up "tto_fp16_op"), a dtype
+//    change that must reallocate, and "attention_haft_op" against the direct
+//    call, bit for bit.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -18,6 +23,7 @@
 #include <vector>
 
 #include "llmx/cuda/attention/attention_api.h"
+#include "llmx/ops.h"
 #include "llmx/tensor.h"
 
 using namespace llmx;
@@ -136,11 +142,121 @@ static void argument_errors_throw() {
   EXPECT(threw);
 }
 
+static void registry_conversions() {
+  Device cpu(DeviceType::kCPU), gpu(DeviceType::kCUDA, 0);
+  // ops_test.cpp: fp16 [1, 2, 3, 4] -> fp32.  The input starts on the host;
+  // the executor moves it to the device.
+  Tensor input({4}, ScalarType::kFP16, cpu);
+  for (int i = 0; i < 4; ++i) input.data_ptr<__half>()[i] = __float2half(float(i + 1));
+  Tensor output;
+  to_fp32(output, input);
+  EXPECT(cudaDeviceSynchronize() == cudaSuccess);
+  EXPECT(output.is_valid() && output.dtype() == ScalarType::kFP32);
+  EXPECT(output.dims() == std::vector<int>{4} && output.device() == gpu);
+  EXPECT(input.device() == gpu);
+  std::vector<float> f(4);
+  llmx_copy(gpu, cpu, output.const_data_ptr(), f.data(), 16);
+  for (int i = 0; i < 4; ++i) EXPECT(f[i] == float(i + 1));
+
+  // fp32 -> fp16 / bf16 of values that need rounding, 1000 + 3 elements so
+  // both the vector body and the tail run; checked against the host casts.
+  const int n = 1003;
+  Tensor src({n}, ScalarType::kFP32, cpu);
+  for (int i = 0; i < n; ++i) src.data_ptr<float>()[i] = (i - 500) * 0.0123457f + 1e-4f * (i % 7);
+  std::vector<float> host(src.const_data_ptr<float>(), src.const_data_ptr<float>() + n);
+  Tensor h16, b16;
+  to_fp16(h16, src);
+  to_bf16(b16, src);
+  EXPECT(cudaDeviceSynchronize() == cudaSuccess);
+  std::vector<__half> gh(n);
+  std::vector<__nv_bfloat16> gb(n);
+  llmx_copy(gpu, cpu, h16.const_data_ptr(), gh.data(), n * 2);
+  llmx_copy(gpu, cpu, b16.const_data_ptr(), gb.data(), n * 2);
+  int bad = 0;
+  for (int i = 0; i < n; ++i) {
+    const __half eh = __float2half_rn(host[i]);
+    const __nv_bfloat16 eb = __float2bfloat16_rn(host[i]);
+    bad += std::memcmp(&eh, &gh[i], 2) != 0;
+    bad += std::memcmp(&eb, &gb[i], 2) != 0;
+  }
+  EXPECT(bad == 0);
+
+  // An output reused at a wider dtype must get new storage.
+  Tensor out2;
+  to_fp16(out2, src);
+  const size_t narrow = out2.nbytes();
+  to_fp32(out2, h16);
+  EXPECT(out2.nbytes() >= size_t(n) * 4 && out2.nbytes() > narrow);
+  EXPECT(cudaDeviceSynchronize() == cudaSuccess);
+
+  bool threw = false;
+  try {
+    get_op_executor()->run("tto_fp16_op", {{"input", &src}, {"output", &out2}}, {});
+  } catch (const std::runtime_error &) {
+    threw = true;
+  }
+  EXPECT(threw);
+}
+
+static void registry_attention_matches_direct_call() {
+  const int S = 300, H = 8, Hkv = 2, D = 128;
+  Device gpu(DeviceType::kCUDA, 0), cpu(DeviceType::kCPU);
+  std::vector<__half> hq(S * H * D), hk(S * Hkv * D), hv(S * Hkv * D);
+  unsigned s = 777u;
+  auto rnd = [&] {
+    s = s * 1664525u + 1013904223u;
+    return float((s >> 8) & 0xffff) / 32768.f - 1.f;
+  };
+  for (auto &x : hq) x = __float2half(rnd());
+  for (auto &x : hk) x = __float2half(rnd());
+  for (auto &x : hv) x = __float2half(rnd());
+  Tensor q({S, H, D}, ScalarType::kFP16, gpu), k({S, Hkv, D}, ScalarType::kFP16, gpu),
+      v({S, Hkv, D}, ScalarType::kFP16, gpu), direct({S, H, D}, ScalarType::kFP16, gpu);
+  llmx_copy(cpu, gpu, hq.data(), q.data_ptr(), q.nbytes());
+  llmx_copy(cpu, gpu, hk.data(), k.data_ptr(), k.nbytes());
+  llmx_copy(cpu, gpu, hv.data(), v.data_ptr(), v.nbytes());
+  std::vector<float> hs(H);
+  for (int h = 0; h < H; ++h) hs[h] = std::exp2(-8.f * (h + 1) / H);
+  Tensor slopes_cpu(hs.data(), {H}, ScalarType::kFP32, cpu);
+  Tensor slopes({H}, ScalarType::kFP32, gpu);
+  llmx_copy(cpu, gpu, hs.data(), slopes.data_ptr(), slopes.nbytes());
+  const float scale = 1.f / std::sqrt(float(D));
+  llmx_single_mha_attention(direct, q, k, v, slopes, scale, 100, 0.f);
+  Tensor via_registry;
+  Parameters params{{"alibi_slopes", std::optional<Tensor>(slopes_cpu)},  // host slopes are moved
+                    {"sm_scale", scale},
+                    {"sliding_window", 100},
+                    {"logits_soft_cap", 0.f}};
+  get_op_executor()->run("attention_haft_op",
+                         {{"query", &q}, {"key", &k}, {"value", &v}, {"output", &via_registry}}, params);
+  Tensor via_helper;
+  attention(via_helper, q, k, v, slopes, scale, 100, 0.f);
+  EXPECT(cudaDeviceSynchronize() == cudaSuccess);
+  EXPECT(via_registry.dims() == q.dims() && via_registry.dtype() == ScalarType::kFP16);
+  std::vector<__half> a(direct.numel()), b(direct.numel()), c(direct.numel());
+  llmx_copy(gpu, cpu, direct.const_data_ptr(), a.data(), a.size() * 2);
+  llmx_copy(gpu, cpu, via_registry.const_data_ptr(), b.data(), b.size() * 2);
+  llmx_copy(gpu, cpu, via_helper.const_data_ptr(), c.data(), c.size() * 2);
+  EXPECT(std::memcmp(a.data(), b.data(), a.size() * 2) == 0);
+  EXPECT(std::memcmp(a.data(), c.data(), a.size() * 2) == 0);
+  // Host tensors handed to the direct call are refused, not dereferenced.
+  bool threw = false;
+  try {
+    Tensor hq_t(hq.data(), {S, H, D}, ScalarType::kFP16, cpu);
+    llmx_single_mha_attention(direct, hq_t, k, v, std::nullopt, scale);
+  } catch (const std::runtime_error &) {
+    threw = true;
+  }
+  EXPECT(threw);
+}
+
 int main() {
   tensor_semantics();
   smoke_zero_inputs();
   known_answer_uniform_weights();
   argument_errors_throw();
+  registry_conversions();
+  registry_attention_matches_direct_call();
   if (g_fail) {
     std::fprintf(stderr, "%d check(s) failed\n", g_fail);
     return 1;
