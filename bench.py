@@ -323,6 +323,40 @@ def bench_kv_split(steps, warmup, rank, world, device, stream, peaks):
                          "frac": fl / world / (per * 1e-3) / 1e12 / peaks["bf16_tflops"]}}
 
 
+def bench_convert(steps, warmup, rank, world, device, stream, peaks):
+    """The dtype-convert op (to_bf16 of an fp32 tensor, 256 Mi elements = 1 GiB
+    in, 512 MiB out; both larger than L2): HBM-bound, bytes read + written."""
+    import llmx_b200
+
+    n = 256 << 20
+    g = torch.Generator(device=device).manual_seed(7 + rank)
+    x = torch.randn(n, generator=g, device=device)
+    out = torch.empty(n, dtype=torch.bfloat16, device=device)
+    times = []
+    with torch.cuda.stream(stream):
+        for i in range(warmup + steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            llmx_b200.convert(x, torch.bfloat16, out=out)
+            e1.record(stream)
+            if i >= warmup:
+                times.append((e0, e1))
+    stream.synchronize()
+    ms = [a.elapsed_time(b) for a, b in times]
+    t = torch.tensor([sum(ms)], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    nbytes = n * (4 + 2)
+    per = float(t.item()) / steps
+    achieved = nbytes / (statistics.mean(ms) * 1e-3) / 1e9
+    del x, out
+    return {"kernel": "convert", "value": nbytes * world / (per * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": per,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": None, "algorithmic": nbytes}}
+
+
 def run_ours(args):
     rank, world, local = dist_info()
     device = torch.device("cuda", local)
@@ -349,6 +383,9 @@ def run_ours(args):
             r, _, _ = bench_workload(name, steps, min(args.warmup, 3) if name.startswith("long_") else args.warmup,
                                      rank, world, device, stream, peaks, False)
             extras[name] = {k: r[k] for k in ("kernel", "value", "unit", "ms_per_step", "roofline")}
+    if not args.no_extra:
+        extras["dtype_convert_fp32_to_bf16_256Mi"] = bench_convert(args.steps, args.warmup, rank, world, device,
+                                                                   stream, peaks)
     if world > 1 and not args.no_extra:
         extras["long_prefill_kv_split_" + str(world) + "gpu"] = bench_kv_split(
             3, min(args.warmup, 3), rank, world, device, stream, peaks)

@@ -56,11 +56,12 @@ constexpr int kBN = 128;       // keys per KV block
 constexpr int kThreads = 384;  // 2 softmax warpgroups + MMA / TMA warpgroup
 constexpr int kMmaWarp = 8;
 constexpr int kTmaWarp = 9;
-// Register split (setmaxnreg): the CTA launches with 384 x 168; the MMA / TMA
-// warpgroup gives back down to 80 and the softmax warpgroups grow to 208:
-// 128 * 80 + 256 * 208 = 63488 <= 384 * 168 = 64512.
-constexpr uint32_t kRegsControl = 80;
-constexpr uint32_t kRegsSoftmax = 208;
+// Register split (setmaxnreg, multiples of 8): the CTA launches with 384 x 168;
+// the MMA / TMA warpgroup drops to 104 (the lowest count at which the MMA
+// issue loop does not spill) and the softmax warpgroups grow to 200:
+// 128 * 104 + 256 * 200 = 64512 = 384 * 168.
+constexpr uint32_t kRegsControl = 104;
+constexpr uint32_t kRegsSoftmax = 200;
 static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * 168, "register split exceeds the launch");
 constexpr uint64_t kTimeoutNs = 1000000000ull;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -295,6 +296,21 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&v)[32], int c0, int 
   float m[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) m[i] = -CUDART_INF_F;
+  if constexpr (!kAlibi) {
+    // Without ALiBi the score transform is increasing (scale2 > 0, tanh), so
+    // the row max is the transform of the raw max: one max per column.
+#pragma unroll
+    for (int c = 0; c < 32; c += 2) {
+      float y0 = __uint_as_float(v[c]), y1 = __uint_as_float(v[c + 1]);
+      if (kMask) {
+        y0 = (c0 + c >= lo && c0 + c < hi) ? y0 : -CUDART_INF_F;
+        y1 = (c0 + c + 1 >= lo && c0 + c + 1 < hi) ? y1 : -CUDART_INF_F;
+      }
+      m[(c >> 1) & 3] = fmax3(m[(c >> 1) & 3], y0, y1);
+    }
+    const float raw = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+    return raw == -CUDART_INF_F ? raw : score2<false, kSoftcap>(__float_as_uint(raw), 0, scale2, 0.f, 0.f, cap_in, cap_out);
+  }
 #pragma unroll
   for (int c = 0; c < 32; c += 2) {
     float y0 = score2<kAlibi, kSoftcap>(v[c], c0 + c, scale2, slope2, jf, cap_in, cap_out);
@@ -741,6 +757,9 @@ cudaError_t launch_d(const AttnArgs &a, cudaStream_t s) {
 bool sm100_supports(const AttnArgs &a) {
   if (a.dtype != 1 && a.dtype != 2) return false;
   if (a.D != 64 && a.D != 128) return false;
+  // The softmax takes the row max on raw scores, which needs an increasing
+  // score transform (sm_scale > 0); other scales run on the SIMT kernel.
+  if (!(a.sm_scale > 0.f)) return false;
   auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (!al16(a.q) || !al16(a.k) || !al16(a.v) || !al16(a.o)) return false;
   const long long *st[4] = {a.qs, a.ks, a.vs, a.os};

@@ -136,3 +136,19 @@ def test_reference_signature_checks():
     with pytest.raises(RuntimeError):
         llmx_b200.single_mha_attention_half(torch.empty_like(q), q.cpu(), q.cpu(), q.cpu(), 0.125)
     llmx_b200.device_status(0)
+
+
+def test_non_positive_scale_leaves_the_tensor_core_kernel():
+    # The tensor-core softmax takes its row max on raw scores, which needs
+    # sm_scale > 0; other scales are routed to the SIMT kernel (auto) or
+    # refused (forced), and still match the oracle.
+    q, k, v = rand(1, 200, 2, 64), rand(1, 200, 2, 64, seed=1), rand(1, 200, 2, 64, seed=2)
+    for scale in (-0.125, 0.0):
+        out = torch.empty_like(q)
+        assert llmx_b200.selected_algo(out, q, k, v, scale) == "simt"
+        llmx_b200.single_mha_attention_half(out, q, k, v, scale)
+        torch.cuda.synchronize()
+        ref = oracle.attention_ref(q[0].float().cpu(), k[0].float().cpu(), v[0].float().cpu(), sm_scale=scale)
+        assert_close(out[0], ref, torch.bfloat16, f"scale {scale}")
+        with pytest.raises(llmx_b200.LlmxError):
+            llmx_b200.single_mha_attention_half(out, q, k, v, scale, algo="tcgen05")
