@@ -84,11 +84,12 @@ void llmx_single_mha_attention(Tensor &output, const Tensor &q, const Tensor &k,
   if (alibi_slopes.has_value())
     check(alibi_slopes->dtype() == ScalarType::kFP32 && alibi_slopes->numel() == size_t(q.dim(1)),
           "alibi_slopes must be fp32 [n_heads]");
-  check_status(llmx_single_mha_attention_c(
-      output.data_ptr(), q.const_data_ptr(), k.const_data_ptr(), v.const_data_ptr(),
-      alibi_slopes.has_value() ? alibi_slopes->const_data_ptr<float>() : nullptr, to_abi_dtype(q.dtype()),
-      q.dim(0), k.dim(0), q.dim(1), k.dim(1), q.dim(2), sm_scale, sliding_window, logits_soft_cap,
-      nullptr));
+  // Same request as llmx_single_mha_attention_c, but through the path that
+  // hands the library its workspace (split-KV decode, prefill work queue).
+  MHAOptions opts;
+  opts.sliding_window = sliding_window;
+  opts.logits_soft_cap = logits_soft_cap;
+  llmx_mha_attention(output, q, k, v, alibi_slopes, sm_scale, opts);
 }
 
 void llmx_mha_attention(Tensor &output, const Tensor &q, const Tensor &k, const Tensor &v,

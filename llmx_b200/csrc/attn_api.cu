@@ -257,6 +257,8 @@ llmx_status llmx_attn_workspace_size(const llmx_attn_params *p, size_t *bytes) {
       if (info.ok) a.num_sms = info.num_sms;
     }
     *bytes = plan_decode(a, SIZE_MAX, true).ws_bytes;
+  } else if (algo == LLMX_ALGO_TCGEN05) {
+    *bytes = kSm100WorkspaceBytes;
   }
   return LLMX_OK;
 }
@@ -285,7 +287,7 @@ llmx_status llmx_attn_fwd(const llmx_attn_params *p, void *stream) {
       e = launch_decode(a, plan, p->workspace, st);
       break;
     }
-    case LLMX_ALGO_TCGEN05: e = launch_sm100(a, st); break;
+    case LLMX_ALGO_TCGEN05: e = launch_sm100(a, p->workspace, p->workspace_bytes, st); break;
   }
   if (e != cudaSuccess) return fail(LLMX_ERR_CUDA, std::string("launch failed: ") + cudaGetErrorString(e));
   return LLMX_OK;

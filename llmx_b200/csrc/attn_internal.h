@@ -58,6 +58,11 @@ cudaError_t launch_decode(const AttnArgs &a, const DecodePlan &plan, void *ws, c
 // Returns cudaErrorNotSupported when the request is outside the kernel's
 // envelope (dtype, head_dim, alignment); the caller then picks another path.
 bool sm100_supports(const AttnArgs &a);
-cudaError_t launch_sm100(const AttnArgs &a, cudaStream_t s);
+// Workspace the tensor-core prefill uses for its work counter.  Given at
+// least that much (4-byte aligned), it runs one CTA per SM over a work queue
+// (the counter is zeroed on the stream before the launch); otherwise one CTA
+// per work item.
+constexpr size_t kSm100WorkspaceBytes = 256;
+cudaError_t launch_sm100(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t s);
 
 }  // namespace llmx_b200

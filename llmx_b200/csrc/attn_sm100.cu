@@ -57,13 +57,14 @@ constexpr int kThreads = 384;  // 2 softmax warpgroups + MMA / TMA warpgroup
 constexpr int kMmaWarp = 8;
 constexpr int kTmaWarp = 9;
 // Register split (setmaxnreg, multiples of 8): the CTA launches with 384 x 168;
-// the MMA / TMA warpgroup drops to 104 (the lowest count at which the MMA
-// issue loop does not spill) and the softmax warpgroups grow to 200:
-// 128 * 104 + 256 * 200 = 64512 = 384 * 168.
-constexpr uint32_t kRegsControl = 104;
-constexpr uint32_t kRegsSoftmax = 200;
+// the MMA / TMA warpgroup drops to 64 and the softmax warpgroups grow to 216:
+// 128 * 64 + 256 * 216 = 63488 <= 384 * 168 = 64512.
+constexpr uint32_t kRegsControl = 64;
+constexpr uint32_t kRegsSoftmax = 216;
 static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * 168, "register split exceeds the launch");
 constexpr uint64_t kTimeoutNs = 1000000000ull;
+constexpr int kSchedSlots = 4;
+constexpr int kSchedConsumers = 1 + 8;  // the MMA thread + one lane per softmax warp
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;
@@ -85,10 +86,14 @@ struct Cfg {
 };
 
 struct Bars {
-  uint64_t q_full[2];  // one per query tile
+  uint64_t q_full[2], q_empty[2];  // one per query tile
   uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
   uint64_t s_full[2], p_full[2], o_done[2];
   uint64_t drain;
+  // Work-item ring: the TMA thread publishes each item index (and finally an
+  // index >= n_work) to the MMA thread and the eight softmax warps.
+  uint64_t sched_full[kSchedSlots], sched_empty[kSchedSlots];
+  int sched_w[kSchedSlots];
   uint32_t tmem_base;
   volatile int abort_flag;
 };
@@ -129,74 +134,162 @@ __device__ __forceinline__ BlockRange block_range(const AttnArgs &a, int m0, int
   return r;
 }
 
+// One work item: a (batch, head) unit and a pair of 128-row query tiles.
+struct Work {
+  int h, b, kvh, ql, kl, m0;
+  BlockRange br;
+};
+
+// Work item w in the launch's order: (batch, head) units in groups of
+// `group_units` whose K/V fit in L2 together; inside a group the query-tile
+// pairs go longest first (with causal masking the highest rows see the most
+// keys), so the machine works on one L2-resident K/V set at a time and short
+// items fill the tail.
+__device__ __forceinline__ Work decode_work(const AttnArgs &a, int w, int n_mblocks, int group_units) {
+  const int units = a.B * a.H;
+  const int per_group = group_units * n_mblocks;
+  const int g = w / per_group;
+  const int within = w - g * per_group;
+  const int gu = min(group_units, units - g * group_units);
+  const int rank = within / gu;
+  const int unit = g * group_units + within % gu;
+  const int mblk = a.causal ? (n_mblocks - 1 - rank) : rank;
+  Work t;
+  t.h = unit % a.H;
+  t.b = unit / a.H;
+  t.kvh = t.h / a.group;
+  t.ql = clamp_len(a.q_lens, t.b, a.Sq);
+  t.kl = clamp_len(a.kv_lens, t.b, a.Skv);
+  t.m0 = mblk * (kTiles * kBM);
+  t.br = block_range(a, t.m0, t.ql, t.kl);
+  return t;
+}
+
+// Scheduling.  CTA i starts with item i; with a work counter (persistent
+// launch, one CTA per SM) the TMA thread then takes item G + atomicAdd(ctr, 1)
+// each time it finishes issuing the loads of one, so CTAs that drew short
+// items take more of them; without one (one CTA per item) it stops after
+// its first.  Every item index, and a final one >= n_work, goes through the
+// shared-memory ring to the other roles, so all roles see the same sequence.
+__device__ __forceinline__ bool sched_publish(Bars *bars, int n, int w) {
+  const int slot = n % kSchedSlots;
+  if (n >= kSchedSlots &&
+      !mbar_wait_or_abort(&bars->sched_empty[slot], ((n / kSchedSlots) - 1) & 1, kTimeoutNs, &bars->abort_flag))
+    return false;
+  bars->sched_w[slot] = w;
+  mbar_arrive(&bars->sched_full[slot]);  // release: orders the store above
+  return true;
+}
+
+// The n-th item of the sequence for a consumer role, or -1 on abort.  One
+// thread per consumer (the MMA thread, lane 0 of each softmax warp) arrives
+// on sched_empty once every thread it stands for has read the slot.
+__device__ __forceinline__ int sched_take(Bars *bars, int n, bool warp_wide) {
+  const int slot = n % kSchedSlots;
+  bool ok = mbar_wait_or_abort(&bars->sched_full[slot], (n / kSchedSlots) & 1, kTimeoutNs, &bars->abort_flag);
+  if (warp_wide) ok = __all_sync(0xffffffffu, ok);
+  if (!ok) return -1;
+  const int w = *reinterpret_cast<volatile int *>(&bars->sched_w[slot]);
+  if (warp_wide) __syncwarp();
+  if (!warp_wide || (threadIdx.x % 32) == 0) mbar_arrive(&bars->sched_empty[slot]);
+  return w;
+}
+
+// Loads issued so far by the TMA thread (for the drain before exit).
+struct TmaCounts {
+  int k = 0, v = 0, q[2] = {0, 0};
+};
+
 // ---------------------------------------------------------------- TMA role
+// Loads for one work item: Q tile 0, then per key block K (and after the
+// first K, Q tile 1) and V through the ring.  kv_base is the number of key
+// blocks of earlier items (ring position and phase); a Q buffer is refilled
+// once the previous item's last QK^T on it has completed (q_empty).
 template <int D>
-__device__ void tma_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k, const CUtensorMap *tm_v,
-                         uint8_t *smem, Bars *bars, unsigned int *err, int m0, int h, int kvh, int b,
-                         BlockRange br) {
+__device__ bool tma_tile(const CUtensorMap *tm_q, const CUtensorMap *tm_k, const CUtensorMap *tm_v, uint8_t *smem,
+                         Bars *bars, const Work &t, int tile_it, int kv_base, TmaCounts &n) {
   using C = Cfg<D>;
-  auto load_q = [&](int t) {
-    mbar_arrive_expect_tx(&bars->q_full[t], C::kTileBytes);
-    for (int c = 0; c < C::kChunks; ++c)
-      tma_load_4d(smem + C::kQOff + t * C::kTileBytes + c * C::kChunkBytes, tm_q, &bars->q_full[t], c * 64, h,
-                  m0 + t * kBM, b);
+  auto wait = [&](uint64_t *bar, uint32_t par) {
+    return mbar_wait_or_abort(bar, par, kTimeoutNs, &bars->abort_flag);
   };
-  load_q(0);
-  int issued_k = 0, issued_v = 0;
-  for (int j = 0; j < br.nb; ++j) {
-    const int s = j % C::kStages;
-    const uint32_t par = ((j / C::kStages) & 1) ^ 1;
-    const int n0 = br.n_start + j * kBN;
-    if (!mbar_wait(&bars->k_empty[s], par, kTimeoutNs)) {
-      set_abort(bars, err);
-      break;
-    }
+  auto load_q = [&](int q) {
+    if (tile_it > 0 && !wait(&bars->q_empty[q], (tile_it - 1) & 1)) return false;
+    mbar_arrive_expect_tx(&bars->q_full[q], C::kTileBytes);
+    for (int c = 0; c < C::kChunks; ++c)
+      tma_load_4d(smem + C::kQOff + q * C::kTileBytes + c * C::kChunkBytes, tm_q, &bars->q_full[q], c * 64, t.h,
+                  t.m0 + q * kBM, t.b);
+    n.q[q] = tile_it + 1;
+    return true;
+  };
+  if (!load_q(0)) return false;
+  for (int j = 0; j < t.br.nb; ++j) {
+    const int g = kv_base + j;
+    const int s = g % C::kStages;
+    const uint32_t par = ((g / C::kStages) & 1) ^ 1;
+    const int n0 = t.br.n_start + j * kBN;
+    if (!wait(&bars->k_empty[s], par)) return false;
     mbar_arrive_expect_tx(&bars->k_full[s], C::kTileBytes);
     for (int c = 0; c < C::kChunks; ++c)
-      tma_load_4d(smem + C::kKOff + s * C::kTileBytes + c * C::kChunkBytes, tm_k, &bars->k_full[s], c * 64, kvh,
-                  n0, b);
-    issued_k = j + 1;
-    if (j == 0) load_q(1);
-    if (!mbar_wait(&bars->v_empty[s], par, kTimeoutNs)) {
-      set_abort(bars, err);
-      break;
-    }
+      tma_load_4d(smem + C::kKOff + s * C::kTileBytes + c * C::kChunkBytes, tm_k, &bars->k_full[s], c * 64, t.kvh,
+                  n0, t.b);
+    n.k = g + 1;
+    if (j == 0 && !load_q(1)) return false;
+    if (!wait(&bars->v_empty[s], par)) return false;
     mbar_arrive_expect_tx(&bars->v_full[s], C::kTileBytes);
     for (int c = 0; c < C::kChunks; ++c)
-      tma_load_4d(smem + C::kVOff + s * C::kTileBytes + c * C::kChunkBytes, tm_v, &bars->v_full[s], c * 64, kvh,
-                  n0, b);
-    issued_v = j + 1;
-    if (bars->abort_flag) break;
+      tma_load_4d(smem + C::kVOff + s * C::kTileBytes + c * C::kChunkBytes, tm_v, &bars->v_full[s], c * 64, t.kvh,
+                  n0, t.b);
+    n.v = g + 1;
+    if (bars->abort_flag) return false;
   }
-  // Drain: every load issued must have landed before the CTA may exit.  In a
-  // normal run these phases completed long ago and the waits return at once.
-  mbar_wait(&bars->q_full[0], 0, kTimeoutNs);
-  if (issued_k > 0) mbar_wait(&bars->q_full[1], 0, kTimeoutNs);
-  for (int j = max(0, issued_k - C::kStages); j < issued_k; ++j)
-    mbar_wait(&bars->k_full[j % C::kStages], (j / C::kStages) & 1, kTimeoutNs);
-  for (int j = max(0, issued_v - C::kStages); j < issued_v; ++j)
-    mbar_wait(&bars->v_full[j % C::kStages], (j / C::kStages) & 1, kTimeoutNs);
+  return true;
+}
+
+// Every load issued must have landed before the CTA may exit.  In a normal
+// run these phases completed long ago and the waits return at once.
+template <int D>
+__device__ void tma_drain(Bars *bars, const TmaCounts &n) {
+  using C = Cfg<D>;
+  for (int q = 0; q < 2; ++q)
+    if (n.q[q] > 0) mbar_wait(&bars->q_full[q], (n.q[q] - 1) & 1, kTimeoutNs);
+  for (int g = max(0, n.k - C::kStages); g < n.k; ++g)
+    mbar_wait(&bars->k_full[g % C::kStages], (g / C::kStages) & 1, kTimeoutNs);
+  for (int g = max(0, n.v - C::kStages); g < n.v; ++g)
+    mbar_wait(&bars->v_full[g % C::kStages], (g / C::kStages) & 1, kTimeoutNs);
 }
 
 // ---------------------------------------------------------------- MMA role
+// MMAs of one work item.  kv_base: key blocks of earlier items (ring
+// position); blk_base: the same count for the per-tile barriers (s_full,
+// p_full, o_done complete once per key block); tile_it: earlier items
+// (q_full phase).  The last QK^T on each Q buffer is followed by a commit to
+// q_empty, so the next item's Q load starts while this item finishes.
 template <int D, bool kBF16>
-__device__ void mma_role(uint8_t *smem, Bars *bars, unsigned int *err, uint32_t tmem, BlockRange br) {
+__device__ bool mma_tile(uint8_t *smem, Bars *bars, uint32_t tmem, int nb, int tile_it, int kv_base, int blk_base) {
   using C = Cfg<D>;
   constexpr uint32_t idesc_qk = idesc_f16(128, kBN, kBF16, false);
   constexpr uint32_t idesc_pv = idesc_f16(128, D, kBF16, true);
   const uint32_t q_base = smem_u32(smem + C::kQOff);
   const uint32_t k_base = smem_u32(smem + C::kKOff);
   const uint32_t v_base = smem_u32(smem + C::kVOff);
+  auto wait = [&](uint64_t *bar, uint32_t par) {
+    return mbar_wait_or_abort(bar, par, kTimeoutNs, &bars->abort_flag);
+  };
 
+  // Descriptors are built per call from an opaque base plus the step's
+  // offset in the 14-bit address field (shared addresses < 256 KB, so the
+  // field never carries): the compiler would otherwise keep every stage's
+  // descriptors live in registers across the whole loop.
   // S_t = Q_t K^T over D in steps of 16 (32 bytes inside a 128-byte chunk).
   auto issue_qk = [&](int t, int s) {
     const uint32_t d_tmem = tmem + (t ? C::kTmemS1 : C::kTmemS0);
+    uint64_t da = smem_desc_sw128(q_base + t * C::kTileBytes, 16, 1024);
+    uint64_t db = smem_desc_sw128(k_base + s * C::kTileBytes, 16, 1024);
+    asm volatile("" : "+l"(da), "+l"(db));
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
-      const uint32_t koff = (kk / 4) * C::kChunkBytes + (kk % 4) * 32;
-      const uint64_t da = smem_desc_sw128(q_base + t * C::kTileBytes + koff, 16, 1024);
-      const uint64_t db = smem_desc_sw128(k_base + s * C::kTileBytes + koff, 16, 1024);
-      mma_ss(d_tmem, da, db, idesc_qk, kk > 0 ? 1u : 0u);
+      const uint64_t off = (uint64_t)(((kk / 4) * C::kChunkBytes + (kk % 4) * 32) >> 4);
+      mma_ss(d_tmem, da + off, db + off, idesc_qk, kk > 0 ? 1u : 0u);
     }
   };
   // O_t (+)= P_t V over the 128 keys in steps of 16 (P: 8 TMEM columns per
@@ -204,66 +297,58 @@ __device__ void mma_role(uint8_t *smem, Bars *bars, unsigned int *err, uint32_t 
   auto issue_pv = [&](int t, int s, bool acc) {
     const uint32_t d_tmem = tmem + (t ? C::kTmemO1 : C::kTmemO0);
     const uint32_t p_tmem = tmem + (t ? C::kTmemS1 : C::kTmemS0);
+    uint64_t db = smem_desc_sw128(v_base + s * C::kTileBytes, C::kChunkBytes, 1024);
+    asm volatile("" : "+l"(db));
 #pragma unroll
-    for (int kk = 0; kk < kBN / 16; ++kk) {
-      const uint64_t db = smem_desc_sw128(v_base + s * C::kTileBytes + kk * 16 * 128, C::kChunkBytes, 1024);
-      mma_ts(d_tmem, p_tmem + kk * 8, db, idesc_pv, (acc || kk > 0) ? 1u : 0u);
-    }
+    for (int kk = 0; kk < kBN / 16; ++kk)
+      mma_ts(d_tmem, p_tmem + kk * 8, db + (uint64_t)((kk * 16 * 128) >> 4), idesc_pv, (acc || kk > 0) ? 1u : 0u);
   };
 
-  bool ok = mbar_wait(&bars->q_full[0], 0, kTimeoutNs) && mbar_wait(&bars->k_full[0], 0, kTimeoutNs);
-  if (ok) {
+  const uint32_t qpar = tile_it & 1;
+  const int s0 = kv_base % C::kStages;
+  if (!wait(&bars->q_full[0], qpar) || !wait(&bars->k_full[s0], (kv_base / C::kStages) & 1)) return false;
+  tc_fence_after();
+  issue_qk(0, s0);
+  tc_commit(&bars->s_full[0]);
+  if (nb == 1) tc_commit(&bars->q_empty[0]);
+  if (!wait(&bars->q_full[1], qpar)) return false;
+  tc_fence_after();
+  issue_qk(1, s0);
+  tc_commit(&bars->s_full[1]);
+  tc_commit(&bars->k_empty[s0]);
+  if (nb == 1) tc_commit(&bars->q_empty[1]);
+  for (int j = 0; j < nb; ++j) {
+    const int g = kv_base + j;
+    const int sv = g % C::kStages;
+    const int sk = (g + 1) % C::kStages;
+    const uint32_t bpar = (blk_base + j) & 1;
+    const bool more = j + 1 < nb;
+    const bool last_qk = j + 2 == nb;
+    if (!wait(&bars->v_full[sv], (g / C::kStages) & 1) || !wait(&bars->p_full[0], bpar)) return false;
     tc_fence_after();
-    issue_qk(0, 0);
-    tc_commit(&bars->s_full[0]);
-    ok = mbar_wait(&bars->q_full[1], 0, kTimeoutNs);
-  }
-  if (!ok) set_abort(bars, err);
-  if (ok) {
-    tc_fence_after();
-    issue_qk(1, 0);
-    tc_commit(&bars->s_full[1]);
-    tc_commit(&bars->k_empty[0]);
-    for (int j = 0; j < br.nb; ++j) {
-      const int sv = j % C::kStages;
-      const int sk = (j + 1) % C::kStages;
-      const bool more = j + 1 < br.nb;
-      if (!mbar_wait(&bars->v_full[sv], (j / C::kStages) & 1, kTimeoutNs) ||
-          !mbar_wait(&bars->p_full[0], j & 1, kTimeoutNs)) {
-        set_abort(bars, err);
-        break;
-      }
+    issue_pv(0, sv, j > 0);
+    tc_commit(&bars->o_done[0]);
+    if (more) {
+      if (!wait(&bars->k_full[sk], ((g + 1) / C::kStages) & 1)) return false;
       tc_fence_after();
-      issue_pv(0, sv, j > 0);
-      tc_commit(&bars->o_done[0]);
-      if (more) {
-        if (!mbar_wait(&bars->k_full[sk], ((j + 1) / C::kStages) & 1, kTimeoutNs)) {
-          set_abort(bars, err);
-          break;
-        }
-        tc_fence_after();
-        issue_qk(0, sk);
-        tc_commit(&bars->s_full[0]);
-      }
-      if (!mbar_wait(&bars->p_full[1], j & 1, kTimeoutNs)) {
-        set_abort(bars, err);
-        break;
-      }
-      tc_fence_after();
-      issue_pv(1, sv, j > 0);
-      tc_commit(&bars->o_done[1]);
-      tc_commit(&bars->v_empty[sv]);
-      if (more) {
-        issue_qk(1, sk);
-        tc_commit(&bars->s_full[1]);
-        tc_commit(&bars->k_empty[sk]);
-      }
-      if (bars->abort_flag) break;
+      issue_qk(0, sk);
+      tc_commit(&bars->s_full[0]);
+      if (last_qk) tc_commit(&bars->q_empty[0]);
     }
+    if (!wait(&bars->p_full[1], bpar)) return false;
+    tc_fence_after();
+    issue_pv(1, sv, j > 0);
+    tc_commit(&bars->o_done[1]);
+    tc_commit(&bars->v_empty[sv]);
+    if (more) {
+      issue_qk(1, sk);
+      tc_commit(&bars->s_full[1]);
+      tc_commit(&bars->k_empty[sk]);
+      if (last_qk) tc_commit(&bars->q_empty[1]);
+    }
+    if (bars->abort_flag) return false;
   }
-  // Drain: all MMAs this thread issued complete before tensor memory is freed.
-  tc_commit(&bars->drain);
-  mbar_wait(&bars->drain, 0, kTimeoutNs);
+  return true;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -310,18 +395,19 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&v)[32], int c0, int 
     }
     const float raw = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
     return raw == -CUDART_INF_F ? raw : score2<false, kSoftcap>(__float_as_uint(raw), 0, scale2, 0.f, 0.f, cap_in, cap_out);
-  }
+  } else {
 #pragma unroll
-  for (int c = 0; c < 32; c += 2) {
-    float y0 = score2<kAlibi, kSoftcap>(v[c], c0 + c, scale2, slope2, jf, cap_in, cap_out);
-    float y1 = score2<kAlibi, kSoftcap>(v[c + 1], c0 + c + 1, scale2, slope2, jf, cap_in, cap_out);
-    if (kMask) {
-      y0 = (c0 + c >= lo && c0 + c < hi) ? y0 : -CUDART_INF_F;
-      y1 = (c0 + c + 1 >= lo && c0 + c + 1 < hi) ? y1 : -CUDART_INF_F;
+    for (int c = 0; c < 32; c += 2) {
+      float y0 = score2<kAlibi, kSoftcap>(v[c], c0 + c, scale2, slope2, jf, cap_in, cap_out);
+      float y1 = score2<kAlibi, kSoftcap>(v[c + 1], c0 + c + 1, scale2, slope2, jf, cap_in, cap_out);
+      if (kMask) {
+        y0 = (c0 + c >= lo && c0 + c < hi) ? y0 : -CUDART_INF_F;
+        y1 = (c0 + c + 1 >= lo && c0 + c + 1 < hi) ? y1 : -CUDART_INF_F;
+      }
+      m[(c >> 1) & 3] = fmax3(m[(c >> 1) & 3], y0, y1);
     }
-    m[(c >> 1) & 3] = fmax3(m[(c >> 1) & 3], y0, y1);
+    return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
   }
-  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
 }
 
 // p = 2^(score - m) for 32 columns, packed in pairs into pk[0..15];
@@ -474,12 +560,15 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int kv_offset
 }
 
 // ------------------------------------------------------------ softmax role
-// Thread r of warpgroup t owns query row r of tile t (TMEM lane r).
+// One work item.  Thread r of warpgroup t owns query row r of tile t (TMEM
+// lane r).  blk_base: key blocks of earlier items (barrier phases).  Returns
+// false when the kernel is aborting.
 template <typename T, int D, bool kAlibi, bool kSoftcap>
-__device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int warp, BlockRange br, int m0,
-                             int h, int b, int ql, int kl) {
+__device__ bool softmax_tile(const AttnArgs &a, Bars *bars, uint32_t tmem, int warp, const Work &w, int blk_base) {
   using C = Cfg<D>;
   const float kNegInf = -CUDART_INF_F;
+  const BlockRange br = w.br;
+  const int m0 = w.m0, h = w.h, b = w.b, ql = w.ql, kl = w.kl;
   const int t = warp / 4;
   const int r = threadIdx.x % kBM;
   const int row0 = m0 + t * kBM;
@@ -498,7 +587,7 @@ __device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
 
   for (int j = 0; j < br.nb; ++j) {
     const int n0 = br.n_start + j * kBN;
-    bool ok = mbar_wait(&bars->s_full[t], j & 1, kTimeoutNs);
+    bool ok = mbar_wait_or_abort(&bars->s_full[t], (blk_base + j) & 1, kTimeoutNs, &bars->abort_flag);
     if (!__all_sync(0xffffffffu, ok)) {
       set_abort(bars, a.err);
       aborted = true;
@@ -525,7 +614,7 @@ __device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
                                                 rescale);
     if (__any_sync(0xffffffffu, rescale)) {
       // O_t holds blocks 0..j-1 once PV_t(j-1) is done; rescale it in place.
-      ok = mbar_wait(&bars->o_done[t], (j - 1) & 1, kTimeoutNs);
+      ok = mbar_wait_or_abort(&bars->o_done[t], (blk_base + j - 1) & 1, kTimeoutNs, &bars->abort_flag);
       if (!__all_sync(0xffffffffu, ok)) {
         set_abort(bars, a.err);
         aborted = true;
@@ -550,7 +639,7 @@ __device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
 
   // Epilogue: O_t / l -> global (rows past q_len as zeros), lse.
   if (!aborted && br.nb > 0) {
-    bool ok = mbar_wait(&bars->o_done[t], (br.nb - 1) & 1, kTimeoutNs);
+    bool ok = mbar_wait_or_abort(&bars->o_done[t], (blk_base + br.nb - 1) & 1, kTimeoutNs, &bars->abort_flag);
     if (!__all_sync(0xffffffffu, ok)) {
       set_abort(bars, a.err);
       aborted = true;
@@ -585,44 +674,31 @@ __device__ void softmax_role(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
   }
   if (a.lse != nullptr && qi < a.Sq)
     a.lse[((long long)b * a.H + h) * a.Sq + qi] = valid ? (m_used + log2f(l)) * kLn2 : kNegInf;
+  return !aborted;
 }
 
 // ------------------------------------------------------------------ kernel
+// With a work counter the grid has one CTA per SM and each CTA runs work
+// items back to back, so barrier set-up and tensor-memory allocation happen
+// once per CTA, and the next item's Q / K / V loads and first QK^T overlap
+// the current item's last block and epilogue.  Without one, one CTA per item.
 template <typename T, int D, bool kAlibi, bool kSoftcap>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int n_mblocks,
-                      const int group_units) {
+                      const int group_units, const int n_work, int *work_ctr) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzled tiles want 1024-byte aligned shared-memory addresses.
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars *bars = reinterpret_cast<Bars *>(smem + C::kBarOff);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // Work order: (batch, head) units in groups of `group_units` whose K/V fit
-  // in L2 together; inside a group the query blocks go longest first (with
-  // causal masking the highest rows see the most keys), so the machine works
-  // on one L2-resident K/V set at a time and short blocks fill the tail.
-  int mblk, unit;
-  {
-    const int units = a.B * a.H;
-    const int per_group = group_units * n_mblocks;
-    const int g = (int)blockIdx.x / per_group;
-    const int within = (int)blockIdx.x - g * per_group;
-    const int gu = min(group_units, units - g * group_units);
-    const int rank = within / gu;
-    unit = g * group_units + within % gu;
-    mblk = a.causal ? (n_mblocks - 1 - rank) : rank;
-  }
-  const int h = unit % a.H, b = unit / a.H, kvh = h / a.group;
-  const int ql = clamp_len(a.q_lens, b, a.Sq);
-  const int kl = clamp_len(a.kv_lens, b, a.Skv);
-  const int m0 = mblk * (kTiles * kBM);
-  const BlockRange br = block_range(a, m0, ql, kl);
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->q_full[0], 1);
-    mbar_init(&bars->q_full[1], 1);
+    for (int q = 0; q < kTiles; ++q) {
+      mbar_init(&bars->q_full[q], 1);
+      mbar_init(&bars->q_empty[q], 1);
+    }
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
@@ -633,6 +709,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->s_full[t], 1);
       mbar_init(&bars->p_full[t], kBM);
       mbar_init(&bars->o_done[t], 1);
+    }
+    for (int i = 0; i < kSchedSlots; ++i) {
+      mbar_init(&bars->sched_full[i], 1);
+      mbar_init(&bars->sched_empty[i], kSchedConsumers);
     }
     mbar_init(&bars->drain, 1);
     bars->abort_flag = 0;
@@ -654,15 +734,66 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp >= 8) {
     regs_decrease<kRegsControl>();
-    if (warp == kTmaWarp) {
-      if (lane == 0 && br.nb > 0) tma_role<D>(&tm_q, &tm_k, &tm_v, smem, bars, a.err, m0, h, kvh, b, br);
-    } else if (warp == kMmaWarp) {
-      if (lane == 0 && br.nb > 0)
-        mma_role<D, std::is_same<T, __nv_bfloat16>::value>(smem, bars, a.err, tmem, br);
+    if (warp == kTmaWarp && lane == 0) {
+      TmaCounts n;
+      int kv = 0, it = 0;
+      int w = (int)blockIdx.x;
+      for (int seq = 0;; ++seq) {
+        if (!sched_publish(bars, seq, w)) {
+          set_abort(bars, a.err);
+          break;
+        }
+        if (w >= n_work) break;
+        const Work t = decode_work(a, w, n_mblocks, group_units);
+        if (t.br.nb > 0) {
+          const bool ok = tma_tile<D>(&tm_q, &tm_k, &tm_v, smem, bars, t, it, kv, n);
+          kv += t.br.nb;
+          ++it;
+          if (!ok) {
+            set_abort(bars, a.err);
+            break;
+          }
+        }
+        w = work_ctr != nullptr ? (int)gridDim.x + atomicAdd(work_ctr, 1) : n_work;
+      }
+      tma_drain<D>(bars, n);
+    } else if (warp == kMmaWarp && lane == 0) {
+      int kv = 0, it = 0;
+      for (int seq = 0;; ++seq) {
+        const int w = sched_take(bars, seq, false);
+        if (w < 0) {
+          set_abort(bars, a.err);
+          break;
+        }
+        if (w >= n_work) break;
+        const Work t = decode_work(a, w, n_mblocks, group_units);
+        if (t.br.nb == 0) continue;
+        const bool ok = mma_tile<D, std::is_same<T, __nv_bfloat16>::value>(smem, bars, tmem, t.br.nb, it, kv, kv);
+        kv += t.br.nb;
+        ++it;
+        if (!ok) {
+          set_abort(bars, a.err);
+          break;
+        }
+      }
+      // Drain: all MMAs this thread issued complete before tensor memory is freed.
+      tc_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, kTimeoutNs);
     }
   } else {
     regs_increase<kRegsSoftmax>();
-    softmax_role<T, D, kAlibi, kSoftcap>(a, bars, tmem, warp, br, m0, h, b, ql, kl);
+    int blk = 0;
+    for (int seq = 0;; ++seq) {
+      const int w = sched_take(bars, seq, true);
+      if (w < 0) {
+        set_abort(bars, a.err);
+        break;
+      }
+      if (w >= n_work) break;
+      const Work t = decode_work(a, w, n_mblocks, group_units);
+      if (!softmax_tile<T, D, kAlibi, kSoftcap>(a, bars, tmem, warp, t, blk)) break;
+      blk += t.br.nb;
+    }
   }
 
   tc_fence_before();
@@ -718,7 +849,7 @@ bool make_tile_map(CUtensorMap *m, const void *base, bool bf16, int D, int S, in
 }
 
 template <typename T, int D, bool kAlibi, bool kSoftcap>
-cudaError_t launch_t(const AttnArgs &a, cudaStream_t s) {
+cudaError_t launch_t(const AttnArgs &a, int *work_ctr, cudaStream_t s) {
   using C = Cfg<D>;
   constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap tq, tk, tv;
@@ -735,21 +866,31 @@ cudaError_t launch_t(const AttnArgs &a, cudaStream_t s) {
   if (attr_err != cudaSuccess) return attr_err;
   const long long n_mblocks = (a.Sq + kTiles * kBM - 1) / (kTiles * kBM);
   const long long units = (long long)a.B * a.H;
-  if (n_mblocks * units > 0x7fffffffLL) return cudaErrorInvalidValue;
+  // Item indices, and the counter's final values (up to n_work + 2 * grid), stay in int.
+  if (n_mblocks * units > 0x7fffffffLL - (1 << 20)) return cudaErrorInvalidValue;
   // Units per group: K and V rows of one unit take Skv * D * 4 bytes; keep a
   // group's K/V within about half of the 126 MB L2.
   const long long kv_unit = std::max<long long>(1, (long long)a.Skv * D * 4);
   const int group_units = (int)std::max<long long>(1, std::min<long long>(units, (64ll << 20) / kv_unit));
-  dim3 grid((unsigned)(n_mblocks * units));
-  kern<<<grid, kThreads, C::kSmemBytes, s>>>(tq, tk, tv, a, (int)n_mblocks, group_units);
+  const long long n_work = n_mblocks * units;
+  const int sms = std::max(1, a.num_sms);
+  int grid = (int)n_work;
+  if (work_ctr != nullptr && n_work > sms) {
+    cudaError_t e = cudaMemsetAsync(work_ctr, 0, sizeof(int), s);
+    if (e != cudaSuccess) return e;
+    grid = sms;
+  } else {
+    work_ctr = nullptr;
+  }
+  kern<<<grid, kThreads, C::kSmemBytes, s>>>(tq, tk, tv, a, (int)n_mblocks, group_units, (int)n_work, work_ctr);
   return cudaGetLastError();
 }
 
 template <typename T, int D>
-cudaError_t launch_d(const AttnArgs &a, cudaStream_t s) {
+cudaError_t launch_d(const AttnArgs &a, int *ctr, cudaStream_t s) {
   const bool alibi = a.alibi != nullptr, cap = a.softcap > 0.f;
-  if (alibi) return cap ? launch_t<T, D, true, true>(a, s) : launch_t<T, D, true, false>(a, s);
-  return cap ? launch_t<T, D, false, true>(a, s) : launch_t<T, D, false, false>(a, s);
+  if (alibi) return cap ? launch_t<T, D, true, true>(a, ctr, s) : launch_t<T, D, true, false>(a, ctr, s);
+  return cap ? launch_t<T, D, false, true>(a, ctr, s) : launch_t<T, D, false, false>(a, ctr, s);
 }
 
 }  // namespace
@@ -769,10 +910,13 @@ bool sm100_supports(const AttnArgs &a) {
   return true;
 }
 
-cudaError_t launch_sm100(const AttnArgs &a, cudaStream_t s) {
+cudaError_t launch_sm100(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t s) {
   if (!sm100_supports(a)) return cudaErrorNotSupported;
-  if (a.dtype == 1) return a.D == 64 ? launch_d<__half, 64>(a, s) : launch_d<__half, 128>(a, s);
-  return a.D == 64 ? launch_d<__nv_bfloat16, 64>(a, s) : launch_d<__nv_bfloat16, 128>(a, s);
+  int *ctr = (ws != nullptr && ws_bytes >= sizeof(int) && (reinterpret_cast<uintptr_t>(ws) & 3u) == 0)
+                 ? static_cast<int *>(ws)
+                 : nullptr;
+  if (a.dtype == 1) return a.D == 64 ? launch_d<__half, 64>(a, ctr, s) : launch_d<__half, 128>(a, ctr, s);
+  return a.D == 64 ? launch_d<__nv_bfloat16, 64>(a, ctr, s) : launch_d<__nv_bfloat16, 128>(a, ctr, s);
 }
 
 }  // namespace llmx_b200

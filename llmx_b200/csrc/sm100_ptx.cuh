@@ -71,6 +71,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
   }
 }
 
+// As mbar_wait, but also gives up once *abort is non-zero (checked between
+// sleeps): after one role records a timeout, the others stop within one
+// sleep interval instead of each waiting out its own limit.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parity, uint64_t timeout_ns,
+                                                   const volatile int *abort) {
+  constexpr uint32_t kSleepNs = 100000;
+  if (mbar_try_wait(bar, parity, kSleepNs)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity, kSleepNs)) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > timeout_ns) return false;
+  }
+}
+
 // ------------------------------------------------------------------- TMA
 // 4-D tiled load global -> shared, completion counted on `bar` in bytes.
 // Coordinates are element indices in the tensor map's dimension order,

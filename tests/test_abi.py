@@ -133,8 +133,11 @@ def test_workspace_size_for_split_kv_decode():
     assert lib.llmx_attn_workspace_size(ctypes.byref(p), ctypes.byref(ws)) == 0
     # 16 splits of 256 keys: partial O and lse in fp32 for every (split, b, h)
     assert ws.value == 16 * 64 * 32 * (128 + 1) * 4
+    # the tensor-core prefill asks for its work counter (256 bytes); SIMT for nothing
     p2 = _params()
-    assert lib.llmx_attn_workspace_size(ctypes.byref(p2), ctypes.byref(ws)) == 0 and ws.value == 0
+    assert lib.llmx_attn_workspace_size(ctypes.byref(p2), ctypes.byref(ws)) == 0 and ws.value == 256
+    p3 = _params(dtype=0)
+    assert lib.llmx_attn_workspace_size(ctypes.byref(p3), ctypes.byref(ws)) == 0 and ws.value == 0
 
 
 def test_status_strings():

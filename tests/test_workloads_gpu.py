@@ -118,3 +118,24 @@ def test_long_prefill_workload_blocks():
                                        causal=True)
             assert_close(out[0, i0:i1, h], ref[:, 0], w.dtype, f"long prefill h={h} rows {i0}:{i1}")
     llmx_b200.device_status(0)
+
+
+@pytest.mark.parametrize("name", ["llama7b_prefill_bf16_b8_h32_s2048_d128", "padded_prefill_fp16_b4_h16_s1024_d64"])
+def test_prefill_schedule_invariance(name):
+    """The tensor-core prefill runs one CTA per SM over a work queue when it
+    gets a workspace and one CTA per work item without one; every item is
+    computed the same way in both, so the outputs are bit-identical."""
+    import ctypes
+
+    from llmx_b200 import _lib, ops
+
+    w = WORKLOADS[name]
+    inp = make_inputs(w, "cuda")
+    queued = run(w, inp)
+    per_item = torch.empty_like(inp.q)
+    p, keep = ops.build_params(per_item, inp.q, inp.k, inp.v, w.sm_scale, alibi_slopes=inp.alibi, causal=w.causal,
+                               q_lens=inp.q_lens, kv_lens=inp.kv_lens, algo="tcgen05")
+    assert p.workspace is None or p.workspace == 0
+    _lib.check(_lib.load().llmx_attn_fwd(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    assert torch.equal(queued, per_item)
