@@ -78,8 +78,13 @@ struct Cfg {
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kTiles * kTileBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
-  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
+  // ALiBi operands of the extra QK^T step (K-major, no swizzle, 4 KB used
+  // of 8 KB each): A' per query tile, B' shared.
+  static constexpr int kXOff = kVOff + kStages * kTileBytes;
+  static constexpr int kXBytes = 8192;
+  static constexpr int kBarOff = kXOff + 3 * kXBytes;
   static constexpr int kSmemBytes = kBarOff + 1024 + 1024;  // barriers + alignment slack
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
   static constexpr uint32_t kTmemS0 = 0, kTmemS1 = 128;
   static constexpr uint32_t kTmemO0 = 256, kTmemO1 = 256 + D;
   static constexpr uint32_t kTmemCols = 512;
@@ -195,6 +200,20 @@ __device__ __forceinline__ int sched_take(Bars *bars, int n, bool warp_wide) {
   return w;
 }
 
+// ALiBi folded into QK^T (no soft-cap): one more K = 16 step adds
+// beta * c to S[r][c], beta = slope / sm_scale, c = the key's column in its
+// 128-key block.  A'_t (128 x 16, per query tile) holds beta as three 16-bit
+// parts in columns 0-2 of every row; B' (128 x 16) holds c in columns 0-2 of
+// row c.  Integers below 256 are exact in both 16-bit types and the products
+// are exact in fp32, so S' = S + beta * c to fp32 rounding.  The softmax then
+// treats ALiBi like the plain path plus slope * (n0 + kv_offset) per block.
+// Byte offset of element (r, k) in the no-swizzle K-major layout used for
+// A' and B': 8-row x 16-byte core matrices, 128 bytes apart along K,
+// 256 bytes apart between 8-row groups.
+__device__ __forceinline__ int x_offset(int r, int k) {
+  return (r >> 3) * 256 + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2;
+}
+
 // Loads issued so far by the TMA thread (for the drain before exit).
 struct TmaCounts {
   int k = 0, v = 0, q[2] = {0, 0};
@@ -205,15 +224,23 @@ struct TmaCounts {
 // first K, Q tile 1) and V through the ring.  kv_base is the number of key
 // blocks of earlier items (ring position and phase); a Q buffer is refilled
 // once the previous item's last QK^T on it has completed (q_empty).
-template <int D>
+// With kFold the thread also writes the item's ALiBi row (beta: the slope
+// over sm_scale as three 16-bit parts) into A'_q before signalling Q_q.
+template <int D, bool kFold>
 __device__ bool tma_tile(const CUtensorMap *tm_q, const CUtensorMap *tm_k, const CUtensorMap *tm_v, uint8_t *smem,
-                         Bars *bars, const Work &t, int tile_it, int kv_base, TmaCounts &n) {
+                         Bars *bars, const Work &t, int tile_it, int kv_base, TmaCounts &n, uint4 beta) {
   using C = Cfg<D>;
   auto wait = [&](uint64_t *bar, uint32_t par) {
     return mbar_wait_or_abort(bar, par, kTimeoutNs, &bars->abort_flag);
   };
   auto load_q = [&](int q) {
     if (tile_it > 0 && !wait(&bars->q_empty[q], (tile_it - 1) & 1)) return false;
+    if constexpr (kFold) {
+      uint8_t *xa = smem + C::kXOff + q * C::kXBytes;
+#pragma unroll 8
+      for (int r = 0; r < kBM; ++r) *reinterpret_cast<uint4 *>(xa + x_offset(r, 0)) = beta;
+      fence_proxy_async_smem();
+    }
     mbar_arrive_expect_tx(&bars->q_full[q], C::kTileBytes);
     for (int c = 0; c < C::kChunks; ++c)
       tma_load_4d(smem + C::kQOff + q * C::kTileBytes + c * C::kChunkBytes, tm_q, &bars->q_full[q], c * 64, t.h,
@@ -264,7 +291,7 @@ __device__ void tma_drain(Bars *bars, const TmaCounts &n) {
 // p_full, o_done complete once per key block); tile_it: earlier items
 // (q_full phase).  The last QK^T on each Q buffer is followed by a commit to
 // q_empty, so the next item's Q load starts while this item finishes.
-template <int D, bool kBF16>
+template <int D, bool kBF16, bool kFold>
 __device__ bool mma_tile(uint8_t *smem, Bars *bars, uint32_t tmem, int nb, int tile_it, int kv_base, int blk_base) {
   using C = Cfg<D>;
   constexpr uint32_t idesc_qk = idesc_f16(128, kBN, kBF16, false);
@@ -272,6 +299,7 @@ __device__ bool mma_tile(uint8_t *smem, Bars *bars, uint32_t tmem, int nb, int t
   const uint32_t q_base = smem_u32(smem + C::kQOff);
   const uint32_t k_base = smem_u32(smem + C::kKOff);
   const uint32_t v_base = smem_u32(smem + C::kVOff);
+  const uint32_t x_base = smem_u32(smem + C::kXOff);
   auto wait = [&](uint64_t *bar, uint32_t par) {
     return mbar_wait_or_abort(bar, par, kTimeoutNs, &bars->abort_flag);
   };
@@ -290,6 +318,13 @@ __device__ bool mma_tile(uint8_t *smem, Bars *bars, uint32_t tmem, int nb, int t
     for (int kk = 0; kk < D / 16; ++kk) {
       const uint64_t off = (uint64_t)(((kk / 4) * C::kChunkBytes + (kk % 4) * 32) >> 4);
       mma_ss(d_tmem, da + off, db + off, idesc_qk, kk > 0 ? 1u : 0u);
+    }
+    if constexpr (kFold) {
+      // S_t += A'_t B'^T: + beta * c for key column c (the ALiBi slope over sm_scale).
+      uint64_t dx = smem_desc_noswz(x_base + t * C::kXBytes, 128, 256);
+      uint64_t dk = smem_desc_noswz(x_base + 2 * C::kXBytes, 128, 256);
+      asm volatile("" : "+l"(dx), "+l"(dk));
+      mma_ss(d_tmem, dx, dk, idesc_qk, 1u);
     }
   };
   // O_t (+)= P_t V over the 128 keys in steps of 16 (P: 8 TMEM columns per
@@ -432,79 +467,6 @@ __device__ __forceinline__ float chunk_exp(const uint32_t (&v)[32], uint32_t (&p
   return (s[0] + s[1]) + (s[2] + s[3]);
 }
 
-// Packed fp32 pairs (sm_100 f32x2 arithmetic): two scores per instruction.
-__device__ __forceinline__ uint64_t f2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void f2_split(uint64_t v, float &lo, float &hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
-// ALiBi path with packed fp32 pairs: the bias slope * (jf + c) is carried
-// pairwise with one f32x2 add, and score * scale + bias (- m) is one f32x2
-// FMA per pair, halving the arithmetic the bias would otherwise add.
-template <bool kMask>
-__device__ __forceinline__ float chunk_max_alibi(const uint32_t (&v)[32], int c0, int lo, int hi, float scale2,
-                                                 float slope2, float jf) {
-  float m[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) m[i] = -CUDART_INF_F;
-  const uint64_t sc = f2(scale2, scale2), step = f2(2.f * slope2, 2.f * slope2);
-  uint64_t bias = f2(slope2 * (jf + (float)c0), slope2 * (jf + (float)(c0 + 1)));
-#pragma unroll
-  for (int c = 0; c < 32; c += 2) {
-    float y0, y1;
-    f2_split(fma2(f2(__uint_as_float(v[c]), __uint_as_float(v[c + 1])), sc, bias), y0, y1);
-    bias = add2(bias, step);
-    if (kMask) {
-      y0 = (c0 + c >= lo && c0 + c < hi) ? y0 : -CUDART_INF_F;
-      y1 = (c0 + c + 1 >= lo && c0 + c + 1 < hi) ? y1 : -CUDART_INF_F;
-    }
-    m[(c >> 1) & 3] = fmax3(m[(c >> 1) & 3], y0, y1);
-  }
-  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
-}
-
-template <typename T, bool kMask>
-__device__ __forceinline__ float chunk_exp_alibi(const uint32_t (&v)[32], uint32_t (&pk)[16], int c0, int lo, int hi,
-                                                 float scale2, float slope2, float jf, float m) {
-  uint64_t acc0 = f2(0.f, 0.f), acc1 = f2(0.f, 0.f);
-  const uint64_t sc = f2(scale2, scale2), step = f2(2.f * slope2, 2.f * slope2);
-  uint64_t off = f2(slope2 * (jf + (float)c0) - m, slope2 * (jf + (float)(c0 + 1)) - m);
-#pragma unroll
-  for (int c = 0; c < 32; c += 2) {
-    float y0, y1;
-    f2_split(fma2(f2(__uint_as_float(v[c]), __uint_as_float(v[c + 1])), sc, off), y0, y1);
-    off = add2(off, step);
-    if (kMask) {
-      y0 = (c0 + c >= lo && c0 + c < hi) ? y0 : -CUDART_INF_F;
-      y1 = (c0 + c + 1 >= lo && c0 + c + 1 < hi) ? y1 : -CUDART_INF_F;
-    }
-    const float p0 = ex2_approx(y0), p1 = ex2_approx(y1);
-    if ((c >> 1) & 1)
-      acc1 = add2(acc1, f2(p0, p1));
-    else
-      acc0 = add2(acc0, f2(p0, p1));
-    pk[c / 2] = pack2<T>(p0, p1);
-  }
-  float a, b, cc, d;
-  f2_split(acc0, a, b);
-  f2_split(acc1, cc, d);
-  return (a + b) + (cc + d);
-}
-
 // One KV block of one row: load S (128 columns, one TMEM round trip), row
 // max, the rescale decision, P = 2^(s - m) written back over S as 16-bit
 // pairs, and the running sum.  kMask selects the per-column interval test;
@@ -520,6 +482,12 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int kv_offset
   // 128 per-column products slope * c out of the block loop into registers.
   float sl = slope2;
   asm volatile("" : "+f"(sl));
+  // ALiBi without soft-cap is folded into S (the per-column part beta * c,
+  // see x_offset); what is left is one constant per block, added to the max
+  // and taken out of the exponent's offset.  kCol: per-column bias here.
+  constexpr bool kFold = kAlibi && !kSoftcap;
+  constexpr bool kCol = kAlibi && !kFold;
+  const float off = kFold ? sl * jf : 0.f;
   uint32_t sr[4][32];
 #pragma unroll
   for (int q = 0; q < 4; ++q) tmem_ld32(tS + q * 32, sr[q]);
@@ -529,10 +497,8 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int kv_offset
   float mx = kNegInf;
 #pragma unroll
   for (int q = 0; q < 4; ++q)
-    if constexpr (kAlibi && !kSoftcap)
-      mx = fmaxf(mx, chunk_max_alibi<kMask>(sr[q], q * 32, lo, hi, scale2, sl, jf));
-    else
-      mx = fmaxf(mx, chunk_max<kAlibi, kSoftcap, kMask>(sr[q], q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out));
+    mx = fmaxf(mx, chunk_max<kCol, kSoftcap, kMask>(sr[q], q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out));
+  if constexpr (kFold) mx += off;  // -inf stays -inf
   // Fresh names for the raw scores: pass 2 recomputes each transformed
   // score instead of keeping pass 1's values alive next to the raw row.
 #pragma unroll
@@ -550,10 +516,8 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int kv_offset
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint32_t pk[16];
-    if constexpr (kAlibi && !kSoftcap)
-      psum += chunk_exp_alibi<T, kMask>(sr[q], pk, q * 32, lo, hi, scale2, sl, jf, m_eff);
-    else
-      psum += chunk_exp<T, kAlibi, kSoftcap, kMask>(sr[q], pk, q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out, m_eff);
+    psum += chunk_exp<T, kCol, kSoftcap, kMask>(sr[q], pk, q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out,
+                                              m_eff - off);
     tmem_st16(tS + q * 16, pk);
   }
   l = l * alpha + psum;
@@ -718,6 +682,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     bars->abort_flag = 0;
     fence_mbar_init();
   }
+  constexpr bool kFold = kAlibi && !kSoftcap;
+  if constexpr (kFold) {
+    // B' row c = [c, c, c, 0, ...] in columns 0-15; A'_0 and A'_1 zero (their
+    // columns 0-2 are written per work item).  256 16-byte units per operand.
+    for (int u = threadIdx.x; u < 3 * 256; u += kThreads) {
+      const int op = u >> 8, e = u & 255;
+      const int r = (e >> 4) * 8 + (e & 7), khalf = (e >> 3) & 1;
+      const float c = (op == 2 && khalf == 0) ? (float)r : 0.f;
+      const float f[8] = {c, c, c, 0.f, 0.f, 0.f, 0.f, 0.f};
+      *reinterpret_cast<uint4 *>(smem + C::kXOff + op * C::kXBytes + x_offset(r, khalf * 8)) = pack8<T>(f);
+    }
+    fence_proxy_async_smem();
+  }
   if (warp == kTmaWarp && lane == 0) {
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
@@ -746,7 +723,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (w >= n_work) break;
         const Work t = decode_work(a, w, n_mblocks, group_units);
         if (t.br.nb > 0) {
-          const bool ok = tma_tile<D>(&tm_q, &tm_k, &tm_v, smem, bars, t, it, kv, n);
+          uint4 beta = make_uint4(0u, 0u, 0u, 0u);
+          if constexpr (kFold) {
+            // beta = slope / sm_scale as three 16-bit parts (each the rounding
+            // of what the previous ones leave), in columns 0-2.
+            const float b = a.alibi[t.h] / a.sm_scale;
+            const float r1 = b - Elem<T>::to_f(Elem<T>::from_f(b));
+            const float r2 = r1 - Elem<T>::to_f(Elem<T>::from_f(r1));
+            const float f[8] = {b, r1, r2, 0.f, 0.f, 0.f, 0.f, 0.f};
+            beta = pack8<T>(f);
+          }
+          const bool ok = tma_tile<D, kFold>(&tm_q, &tm_k, &tm_v, smem, bars, t, it, kv, n, beta);
           kv += t.br.nb;
           ++it;
           if (!ok) {
@@ -768,7 +755,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (w >= n_work) break;
         const Work t = decode_work(a, w, n_mblocks, group_units);
         if (t.br.nb == 0) continue;
-        const bool ok = mma_tile<D, std::is_same<T, __nv_bfloat16>::value>(smem, bars, tmem, t.br.nb, it, kv, kv);
+        const bool ok =
+            mma_tile<D, std::is_same<T, __nv_bfloat16>::value, kFold>(smem, bars, tmem, t.br.nb, it, kv, kv);
         kv += t.br.nb;
         ++it;
         if (!ok) {

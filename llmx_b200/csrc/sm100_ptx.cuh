@@ -243,6 +243,25 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr, uint32_t
   return d;
 }
 
+// Shared-memory matrix descriptor, K-major without swizzle: the operand is
+// made of 8-row x 16-byte core matrices (128 contiguous bytes, row r of a
+// core matrix at +16 r); `lbo` is the byte distance between core matrices
+// adjacent along K, `sbo` between adjacent 8-row groups.
+__device__ __forceinline__ uint64_t smem_desc_noswz(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version (sm_100); swizzle field 0 = none
+  return d;
+}
+
+// Orders this thread's ordinary shared-memory stores before later reads of
+// the same bytes by the async proxy (tensor-core operand fetch).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Instruction descriptor, kind::f16 with fp32 accumulation.
 // a_bf16/b_bf16: element type (0 fp16, 1 bf16); b_mn_major: B is MN-major.
 __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool bf16, bool b_mn_major) {
