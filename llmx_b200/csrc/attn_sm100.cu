@@ -409,6 +409,19 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+// Columns of 32 raw scores (c0..c0+31) outside the row's visible interval
+// [lo, hi) become -inf, in place: one bit test and one select per column.
+// Used when the score transform maps -inf to -inf (no soft-cap), so the max
+// and exponent passes then run unmasked (2^-inf = 0).
+__device__ __forceinline__ void mask_chunk(uint32_t (&v)[32], int c0, int lo, int hi) {
+  const int a = min(max(lo - c0, 0), 32), e = min(max(hi - c0, 0), 32);
+  const uint32_t below_e = e >= 32 ? 0xffffffffu : ((1u << e) - 1u);
+  const uint32_t below_a = a >= 32 ? 0xffffffffu : ((1u << a) - 1u);
+  const uint32_t vis = below_e & ~below_a;
+#pragma unroll
+  for (int c = 0; c < 32; ++c) v[c] = (vis & (1u << c)) ? v[c] : 0xff800000u;
+}
+
 // Max of 32 scores (columns c0..c0+31), four independent chains.
 template <bool kAlibi, bool kSoftcap, bool kMask>
 __device__ __forceinline__ float chunk_max(const uint32_t (&v)[32], int c0, int lo, int hi, float scale2,
@@ -494,10 +507,18 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int kv_offset
   tmem_wait_ld();
 #pragma unroll
   for (int q = 0; q < 4; ++q) reg_fence32(sr[q]);
+  // Without soft-cap the mask is applied once, to the raw scores; with it,
+  // after the transform in both passes (tanh(-inf) is not -inf).
+  constexpr bool kMaskRaw = kMask && !kSoftcap;
+  constexpr bool kMaskPass = kMask && kSoftcap;
+  if constexpr (kMaskRaw) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mask_chunk(sr[q], q * 32, lo, hi);
+  }
   float mx = kNegInf;
 #pragma unroll
   for (int q = 0; q < 4; ++q)
-    mx = fmaxf(mx, chunk_max<kCol, kSoftcap, kMask>(sr[q], q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out));
+    mx = fmaxf(mx, chunk_max<kCol, kSoftcap, kMaskPass>(sr[q], q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out));
   if constexpr (kFold) mx += off;  // -inf stays -inf
   // Fresh names for the raw scores: pass 2 recomputes each transformed
   // score instead of keeping pass 1's values alive next to the raw row.
@@ -516,11 +537,46 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int kv_offset
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint32_t pk[16];
-    psum += chunk_exp<T, kCol, kSoftcap, kMask>(sr[q], pk, q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out,
-                                              m_eff - off);
+    psum += chunk_exp<T, kCol, kSoftcap, kMaskPass>(sr[q], pk, q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out,
+                                                  m_eff - off);
     tmem_st16(tS + q * 16, pk);
   }
   l = l * alpha + psum;
+}
+
+// 4 x 4 transpose of 16-byte pieces inside each group of four lanes: on
+// entry u[j] is piece j of this lane's row, on exit u[k] is piece (lane % 4)
+// of row k of the group.  Two rounds of exchanges with lane ^ 2 and lane ^ 1,
+// each swapping the two pieces whose index bit differs from the lane's.
+__device__ __forceinline__ void xchg_unit(uint4 &dst, const uint4 &src, int mask) {
+  dst.x = __shfl_xor_sync(0xffffffffu, src.x, mask);
+  dst.y = __shfl_xor_sync(0xffffffffu, src.y, mask);
+  dst.z = __shfl_xor_sync(0xffffffffu, src.z, mask);
+  dst.w = __shfl_xor_sync(0xffffffffu, src.w, mask);
+}
+__device__ __forceinline__ void transpose_units4(uint4 (&u)[4]) {
+  const int i = threadIdx.x & 3;
+  const bool b1 = (i >> 1) & 1, b0 = i & 1;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const uint4 send = b1 ? u[k] : u[k | 2];
+    uint4 recv;
+    xchg_unit(recv, send, 2);
+    if (b1)
+      u[k] = recv;
+    else
+      u[k | 2] = recv;
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const uint4 send = b0 ? u[2 * k] : u[2 * k + 1];
+    uint4 recv;
+    xchg_unit(recv, send, 1);
+    if (b0)
+      u[2 * k] = recv;
+    else
+      u[2 * k + 1] = recv;
+  }
 }
 
 // ------------------------------------------------------------ softmax role
@@ -570,7 +626,14 @@ __device__ bool softmax_tile(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
     }
     float alpha = 1.f;
     bool rescale = false;
-    if (need_mask)
+    if (need_mask && __all_sync(0xffffffffu, hi <= lo)) {
+      // No row of this warp sees a key of the block: P = 0, m and l unchanged.
+      uint32_t z[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) z[c] = 0u;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tmem_st16(tS + q * 16, z);
+    } else if (need_mask)
       softmax_block<T, kAlibi, kSoftcap, true>(tS, n0, a.kv_offset, lo, hi, scale2, slope2, cap_in, cap_out, m_used, l, alpha,
                                                rescale);
     else
@@ -614,7 +677,11 @@ __device__ bool softmax_tile(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
   const bool have = !aborted && br.nb > 0;
   const bool valid = qi < ql && l > 0.f;  // padded rows and rows with no visible key -> 0
   const float inv = valid ? 1.f / l : 0.f;
-  T *orow = static_cast<T *>(a.o) + b * a.os[0] + (long long)qi * a.os[1] + h * a.os[2];
+  // Each group of four lanes (four consecutive rows) swaps 16-byte pieces so
+  // that every store instruction writes 64 contiguous bytes of 8 rows.
+  const int gi = threadIdx.x & 3;
+  const int qi_group = qi - gi;
+  T *const obase = static_cast<T *>(a.o) + b * a.os[0] + h * a.os[2];
 #pragma unroll 1
   for (int ch = 0; ch < D / 32; ++ch) {
     uint32_t o[32];
@@ -630,10 +697,14 @@ __device__ bool softmax_tile(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
 #pragma unroll
     for (int c = 0; c < 16; ++c)
       w[c] = valid ? pack2<T>(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv) : 0u;
-    if (qi < a.Sq) {
-      uint4 *dst = reinterpret_cast<uint4 *>(orow + ch * 32);
+    uint4 u[4];
 #pragma unroll
-      for (int v4 = 0; v4 < 4; ++v4) dst[v4] = make_uint4(w[4 * v4], w[4 * v4 + 1], w[4 * v4 + 2], w[4 * v4 + 3]);
+    for (int v4 = 0; v4 < 4; ++v4) u[v4] = make_uint4(w[4 * v4], w[4 * v4 + 1], w[4 * v4 + 2], w[4 * v4 + 3]);
+    transpose_units4(u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int row = qi_group + k;
+      if (row < a.Sq) *reinterpret_cast<uint4 *>(obase + (long long)row * a.os[1] + ch * 32 + gi * 8) = u[k];
     }
   }
   if (a.lse != nullptr && qi < a.Sq)
