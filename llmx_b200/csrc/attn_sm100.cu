@@ -31,8 +31,8 @@
 //
 // Online softmax: running max m and sum l per row in log2 units.  The max is
 // only moved (and O rescaled in tensor memory) when a block raises it by more
-// than 8 (a factor 256), so P <= 256 and O rescales are rare; the final
-// O / l is the same softmax.
+// than rescale_threshold (2^64 for bf16, 2^15 for fp16), so O rescales are
+// rare; the final O / l is the same softmax.
 //
 // Every mbarrier wait is bounded (1 s); on expiry the kernel records
 // kDevErrTimeout in the device error word, unwinds all roles, waits (bounded)
@@ -67,7 +67,14 @@ constexpr int kSchedSlots = 4;
 constexpr int kSchedConsumers = 1 + 8;  // the MMA thread + one lane per softmax warp
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
-constexpr float kRescaleThreshold = 8.0f;
+// Lazy rescale: the running max moves (and O is rescaled) only when a block
+// raises it by more than this many log2 units, so P <= 2^threshold.  bf16 P
+// has the fp32 exponent range and O / l accumulate in fp32, so 2^64; fp16 P
+// must stay below 65504, so 2^15.
+template <typename T>
+constexpr float rescale_threshold() {
+  return std::is_same<T, __nv_bfloat16>::value ? 64.0f : 15.0f;
+}
 
 template <int D>
 struct Cfg {
@@ -142,7 +149,8 @@ __device__ __forceinline__ BlockRange block_range(const AttnArgs &a, int m0, int
 // One work item: a (batch, head) unit and a pair of 128-row query tiles.
 struct Work {
   int h, b, kvh, ql, kl, m0;
-  BlockRange br;
+  BlockRange br;  // key blocks of the item (all visible to tile 1)
+  int nb0;        // leading blocks of br that tile 0 (the earlier rows) sees, >= 1
 };
 
 // Work item w in the launch's order: (batch, head) units in groups of
@@ -167,6 +175,13 @@ __device__ __forceinline__ Work decode_work(const AttnArgs &a, int w, int n_mblo
   t.kl = clamp_len(a.kv_lens, t.b, a.Skv);
   t.m0 = mblk * (kTiles * kBM);
   t.br = block_range(a, t.m0, t.ql, t.kl);
+  t.nb0 = t.br.nb;
+  if (a.causal && t.br.nb > 0) {
+    // With causal masking tile 0's last visible key is row m0 + 127's
+    // diagonal; blocks past it are skipped for tile 0 (at least one is kept).
+    const int hi0 = min(t.kl, min(t.m0 + kBM, t.ql) + diag_shift(a, t.ql, t.kl));
+    t.nb0 = max(1, min(t.br.nb, (hi0 - t.br.n_start + kBN - 1) / kBN));
+  }
   return t;
 }
 
@@ -287,12 +302,13 @@ __device__ void tma_drain(Bars *bars, const TmaCounts &n) {
 
 // ---------------------------------------------------------------- MMA role
 // MMAs of one work item.  kv_base: key blocks of earlier items (ring
-// position); blk_base: the same count for the per-tile barriers (s_full,
-// p_full, o_done complete once per key block); tile_it: earlier items
-// (q_full phase).  The last QK^T on each Q buffer is followed by a commit to
+// position); blk_base0 / blk_base1: key blocks of earlier items on tile 0 /
+// tile 1 (s_full, p_full, o_done complete once per block of their tile);
+// tile_it: earlier items (q_full phase).  The last QK^T on each Q buffer is followed by a commit to
 // q_empty, so the next item's Q load starts while this item finishes.
 template <int D, bool kBF16, bool kFold>
-__device__ bool mma_tile(uint8_t *smem, Bars *bars, uint32_t tmem, int nb, int tile_it, int kv_base, int blk_base) {
+__device__ bool mma_tile(uint8_t *smem, Bars *bars, uint32_t tmem, int nb, int nb0, int tile_it, int kv_base,
+                         int blk_base0, int blk_base1) {
   using C = Cfg<D>;
   constexpr uint32_t idesc_qk = idesc_f16(128, kBN, kBF16, false);
   constexpr uint32_t idesc_pv = idesc_f16(128, D, kBF16, true);
@@ -345,32 +361,34 @@ __device__ bool mma_tile(uint8_t *smem, Bars *bars, uint32_t tmem, int nb, int t
   tc_fence_after();
   issue_qk(0, s0);
   tc_commit(&bars->s_full[0]);
-  if (nb == 1) tc_commit(&bars->q_empty[0]);
+  if (nb0 == 1) tc_commit(&bars->q_empty[0]);
   if (!wait(&bars->q_full[1], qpar)) return false;
   tc_fence_after();
   issue_qk(1, s0);
   tc_commit(&bars->s_full[1]);
   tc_commit(&bars->k_empty[s0]);
   if (nb == 1) tc_commit(&bars->q_empty[1]);
+  // Tile 0 (the earlier rows) runs blocks [0, nb0), tile 1 all nb blocks.
   for (int j = 0; j < nb; ++j) {
     const int g = kv_base + j;
     const int sv = g % C::kStages;
     const int sk = (g + 1) % C::kStages;
-    const uint32_t bpar = (blk_base + j) & 1;
     const bool more = j + 1 < nb;
-    const bool last_qk = j + 2 == nb;
-    if (!wait(&bars->v_full[sv], (g / C::kStages) & 1) || !wait(&bars->p_full[0], bpar)) return false;
-    tc_fence_after();
-    issue_pv(0, sv, j > 0);
-    tc_commit(&bars->o_done[0]);
-    if (more) {
-      if (!wait(&bars->k_full[sk], ((g + 1) / C::kStages) & 1)) return false;
+    if (!wait(&bars->v_full[sv], (g / C::kStages) & 1)) return false;
+    if (j < nb0) {
+      if (!wait(&bars->p_full[0], (blk_base0 + j) & 1)) return false;
+      tc_fence_after();
+      issue_pv(0, sv, j > 0);
+      tc_commit(&bars->o_done[0]);
+    }
+    if (more && !wait(&bars->k_full[sk], ((g + 1) / C::kStages) & 1)) return false;
+    if (j + 1 < nb0) {
       tc_fence_after();
       issue_qk(0, sk);
       tc_commit(&bars->s_full[0]);
-      if (last_qk) tc_commit(&bars->q_empty[0]);
+      if (j + 2 == nb0) tc_commit(&bars->q_empty[0]);
     }
-    if (!wait(&bars->p_full[1], bpar)) return false;
+    if (!wait(&bars->p_full[1], (blk_base1 + j) & 1)) return false;
     tc_fence_after();
     issue_pv(1, sv, j > 0);
     tc_commit(&bars->o_done[1]);
@@ -379,7 +397,7 @@ __device__ bool mma_tile(uint8_t *smem, Bars *bars, uint32_t tmem, int nb, int t
       issue_qk(1, sk);
       tc_commit(&bars->s_full[1]);
       tc_commit(&bars->k_empty[sk]);
-      if (last_qk) tc_commit(&bars->q_empty[1]);
+      if (j + 2 == nb) tc_commit(&bars->q_empty[1]);
     }
     if (bars->abort_flag) return false;
   }
@@ -527,7 +545,7 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int kv_offset
   const float m_new = fmaxf(m_used, mx);
   if (m_used == kNegInf) {
     m_used = m_new;  // nothing accumulated yet: O and l are zero
-  } else if (m_new > m_used + kRescaleThreshold) {
+  } else if (m_new > m_used + rescale_threshold<T>()) {
     alpha = ex2_approx(m_used - m_new);
     m_used = m_new;
     rescale = true;
@@ -587,9 +605,10 @@ template <typename T, int D, bool kAlibi, bool kSoftcap>
 __device__ bool softmax_tile(const AttnArgs &a, Bars *bars, uint32_t tmem, int warp, const Work &w, int blk_base) {
   using C = Cfg<D>;
   const float kNegInf = -CUDART_INF_F;
-  const BlockRange br = w.br;
-  const int m0 = w.m0, h = w.h, b = w.b, ql = w.ql, kl = w.kl;
   const int t = warp / 4;
+  BlockRange br = w.br;
+  if (t == 0) br.nb = w.nb0;
+  const int m0 = w.m0, h = w.h, b = w.b, ql = w.ql, kl = w.kl;
   const int r = threadIdx.x % kBM;
   const int row0 = m0 + t * kBM;
   const int qi = row0 + r;
@@ -816,7 +835,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tma_drain<D>(bars, n);
     } else if (warp == kMmaWarp && lane == 0) {
-      int kv = 0, it = 0;
+      int kv = 0, it = 0, blk0 = 0;
       for (int seq = 0;; ++seq) {
         const int w = sched_take(bars, seq, false);
         if (w < 0) {
@@ -826,9 +845,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (w >= n_work) break;
         const Work t = decode_work(a, w, n_mblocks, group_units);
         if (t.br.nb == 0) continue;
-        const bool ok =
-            mma_tile<D, std::is_same<T, __nv_bfloat16>::value, kFold>(smem, bars, tmem, t.br.nb, it, kv, kv);
+        const bool ok = mma_tile<D, std::is_same<T, __nv_bfloat16>::value, kFold>(smem, bars, tmem, t.br.nb, t.nb0,
+                                                                                    it, kv, blk0, kv);
         kv += t.br.nb;
+        blk0 += t.nb0;
         ++it;
         if (!ok) {
           set_abort(bars, a.err);
@@ -851,7 +871,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (w >= n_work) break;
       const Work t = decode_work(a, w, n_mblocks, group_units);
       if (!softmax_tile<T, D, kAlibi, kSoftcap>(a, bars, tmem, warp, t, blk)) break;
-      blk += t.br.nb;
+      blk += warp < 4 ? t.nb0 : t.br.nb;
     }
   }
 
