@@ -498,6 +498,50 @@ __device__ __forceinline__ float chunk_exp(const uint32_t (&v)[32], uint32_t (&p
   return (s[0] + s[1]) + (s[2] + s[3]);
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): two lanes of work per
+// instruction for the scale-and-subtract and the running sum of the plain
+// (and folded-ALiBi) exponent pass.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// p = 2^(v * scale2 - m) for 32 raw scores (masked ones already -inf),
+// packed in pairs into pk[0..15]; returns the sum of the unrounded p.
+template <typename T>
+__device__ __forceinline__ float chunk_exp_plain2(const uint32_t (&v)[32], uint32_t (&pk)[16], float scale2, float m) {
+  uint64_t acc0 = f2(0.f, 0.f), acc1 = f2(0.f, 0.f);
+  const uint64_t sc = f2(scale2, scale2), nm = f2(-m, -m);
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    float y0, y1;
+    f2_split(fma2(f2(__uint_as_float(v[c]), __uint_as_float(v[c + 1])), sc, nm), y0, y1);
+    const float p0 = ex2_approx(y0), p1 = ex2_approx(y1);
+    if ((c >> 1) & 1)
+      acc1 = add2(acc1, f2(p0, p1));
+    else
+      acc0 = add2(acc0, f2(p0, p1));
+    pk[c / 2] = pack2<T>(p0, p1);
+  }
+  float a, b, cc, d;
+  f2_split(acc0, a, b);
+  f2_split(acc1, cc, d);
+  return (a + b) + (cc + d);
+}
+
 // One KV block of one row: load S (128 columns, one TMEM round trip), row
 // max, the rescale decision, P = 2^(s - m) written back over S as 16-bit
 // pairs, and the running sum.  kMask selects the per-column interval test;
@@ -555,8 +599,11 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, int n0, int kv_offset
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint32_t pk[16];
-    psum += chunk_exp<T, kCol, kSoftcap, kMaskPass>(sr[q], pk, q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out,
-                                                  m_eff - off);
+    if constexpr (!kCol && !kSoftcap)
+      psum += chunk_exp_plain2<T>(sr[q], pk, scale2, m_eff - off);
+    else
+      psum += chunk_exp<T, kCol, kSoftcap, kMaskPass>(sr[q], pk, q * 32, lo, hi, scale2, sl, jf, cap_in, cap_out,
+                                                    m_eff - off);
     tmem_st16(tS + q * 16, pk);
   }
   l = l * alpha + psum;
