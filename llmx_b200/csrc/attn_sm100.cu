@@ -110,7 +110,8 @@ struct Bars {
   volatile int abort_flag;
 };
 
-__device__ __forceinline__ void set_abort(Bars *bars, unsigned int *err) {
+template <typename B>
+__device__ __forceinline__ void set_abort(B *bars, unsigned int *err) {
   bars->abort_flag = 1;
   raise_error(err, kDevErrTimeout);
 }
@@ -131,11 +132,12 @@ struct BlockRange {
   int n_start, nb;
 };
 
-__device__ __forceinline__ BlockRange block_range(const AttnArgs &a, int m0, int ql, int kl) {
+// rows: query rows per work item (kTiles * kBM, or kBM for head_dim 256).
+__device__ __forceinline__ BlockRange block_range(const AttnArgs &a, int m0, int ql, int kl, int rows) {
   BlockRange r{0, 0};
   if (m0 >= ql || kl <= 0) return r;
   const int off = diag_shift(a, ql, kl);
-  const int r_last = min(m0 + kTiles * kBM, ql) - 1;
+  const int r_last = min(m0 + rows, ql) - 1;
   const int hi = a.causal ? min(kl, r_last + off + 1) : kl;
   int lo = a.window >= 0 ? max(0, m0 + off - a.window) : 0;
   lo = (lo / kBN) * kBN;
@@ -158,7 +160,8 @@ struct Work {
 // pairs go longest first (with causal masking the highest rows see the most
 // keys), so the machine works on one L2-resident K/V set at a time and short
 // items fill the tail.
-__device__ __forceinline__ Work decode_work(const AttnArgs &a, int w, int n_mblocks, int group_units) {
+__device__ __forceinline__ Work decode_work(const AttnArgs &a, int w, int n_mblocks, int group_units,
+                                            int rows = kTiles * kBM) {
   const int units = a.B * a.H;
   const int per_group = group_units * n_mblocks;
   const int g = w / per_group;
@@ -173,8 +176,8 @@ __device__ __forceinline__ Work decode_work(const AttnArgs &a, int w, int n_mblo
   t.kvh = t.h / a.group;
   t.ql = clamp_len(a.q_lens, t.b, a.Sq);
   t.kl = clamp_len(a.kv_lens, t.b, a.Skv);
-  t.m0 = mblk * (kTiles * kBM);
-  t.br = block_range(a, t.m0, t.ql, t.kl);
+  t.m0 = mblk * rows;
+  t.br = block_range(a, t.m0, t.ql, t.kl, rows);
   t.nb0 = t.br.nb;
   if (a.causal && t.br.nb > 0) {
     // With causal masking tile 0's last visible key is row m0 + 127's
@@ -191,7 +194,8 @@ __device__ __forceinline__ Work decode_work(const AttnArgs &a, int w, int n_mblo
 // items take more of them; without one (one CTA per item) it stops after
 // its first.  Every item index, and a final one >= n_work, goes through the
 // shared-memory ring to the other roles, so all roles see the same sequence.
-__device__ __forceinline__ bool sched_publish(Bars *bars, int n, int w) {
+template <typename B>
+__device__ __forceinline__ bool sched_publish(B *bars, int n, int w) {
   const int slot = n % kSchedSlots;
   if (n >= kSchedSlots &&
       !mbar_wait_or_abort(&bars->sched_empty[slot], ((n / kSchedSlots) - 1) & 1, kTimeoutNs, &bars->abort_flag))
@@ -204,7 +208,8 @@ __device__ __forceinline__ bool sched_publish(Bars *bars, int n, int w) {
 // The n-th item of the sequence for a consumer role, or -1 on abort.  One
 // thread per consumer (the MMA thread, lane 0 of each softmax warp) arrives
 // on sched_empty once every thread it stands for has read the slot.
-__device__ __forceinline__ int sched_take(Bars *bars, int n, bool warp_wide) {
+template <typename B>
+__device__ __forceinline__ int sched_take(B *bars, int n, bool warp_wide) {
   const int slot = n % kSchedSlots;
   bool ok = mbar_wait_or_abort(&bars->sched_full[slot], (n / kSchedSlots) & 1, kTimeoutNs, &bars->abort_flag);
   if (warp_wide) ok = __all_sync(0xffffffffu, ok);
@@ -931,6 +936,452 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ========================================================== head_dim 256
+// One 128-row query tile per work item.  Tensor memory: two S buffers
+// (S_0, S_1: 128 fp32 columns each) and O (256 columns).  The MMA thread
+// keeps QK^T one key block ahead of PV -- QK(0), QK(1), PV(0), QK(2), PV(1),
+// ... -- so the tensor core computes the next scores and the previous PV
+// while the softmax warpgroup works on the current block (at head_dim 256
+// that is ~2960 tensor cycles per block against ~2100 cycles of softmax).
+// Shared memory holds Q and one 64 KB slot each for K and V (plus the ALiBi
+// operands); K and V have their own TMA threads, so a K load never queues
+// behind a V load.
+struct Cfg256 {
+  static constexpr int D = 256;
+  static constexpr int kChunks = D / 64;
+  static constexpr int kChunkBytes = 128 * 128;
+  static constexpr int kTileBytes = 128 * D * 2;
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = kTileBytes;
+  static constexpr int kVOff = 2 * kTileBytes;
+  static constexpr int kXOff = 3 * kTileBytes;  // A' (8 KB) then B' (8 KB)
+  static constexpr int kXBytes = 8192;
+  static constexpr int kBarOff = kXOff + 2 * kXBytes;
+  static constexpr int kSmemBytes = kBarOff + 1024 + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+  static constexpr uint32_t kTmemS0 = 0, kTmemS1 = 128, kTmemO = 256, kTmemCols = 512;
+};
+constexpr int kThreads256 = 256;  // warps 0-3 softmax, 4 MMA, 5 K + Q loads, 6 V loads, 7 idle
+constexpr int kMmaWarp256 = 4, kKWarp256 = 5, kVWarp256 = 6;
+constexpr int kSchedConsumers256 = 1 + 1 + 4;  // MMA thread, V thread, one lane per softmax warp
+
+struct Bars256 {
+  uint64_t q_full, q_empty, k_full, k_empty, v_full, v_empty;
+  uint64_t s_full[2], p_full[2], o_done;
+  uint64_t drain;
+  uint64_t sched_full[kSchedSlots], sched_empty[kSchedSlots];
+  int sched_w[kSchedSlots];
+  uint32_t tmem_base;
+  volatile int abort_flag;
+};
+static_assert(sizeof(Bars256) <= 1024, "barrier region");
+
+// K / Q loads of one item (the K thread); g0: key blocks of earlier items.
+template <bool kFold>
+__device__ bool tma_k256(const CUtensorMap *tm_q, const CUtensorMap *tm_k, uint8_t *smem, Bars256 *bars,
+                         const Work &t, int tile_it, int g0, int &k_issued, int &q_issued, uint4 beta) {
+  using C = Cfg256;
+  auto wait = [&](uint64_t *bar, uint32_t par) {
+    return mbar_wait_or_abort(bar, par, kTimeoutNs, &bars->abort_flag);
+  };
+  if (tile_it > 0 && !wait(&bars->q_empty, (tile_it - 1) & 1)) return false;
+  if constexpr (kFold) {
+    uint8_t *xa = smem + C::kXOff;
+#pragma unroll 8
+    for (int r = 0; r < kBM; ++r) *reinterpret_cast<uint4 *>(xa + x_offset(r, 0)) = beta;
+    fence_proxy_async_smem();
+  }
+  mbar_arrive_expect_tx(&bars->q_full, C::kTileBytes);
+  for (int c = 0; c < C::kChunks; ++c)
+    tma_load_4d(smem + C::kQOff + c * C::kChunkBytes, tm_q, &bars->q_full, c * 64, t.h, t.m0, t.b);
+  q_issued = tile_it + 1;
+  for (int j = 0; j < t.br.nb; ++j) {
+    const int g = g0 + j;
+    if (!wait(&bars->k_empty, (g & 1) ^ 1)) return false;
+    mbar_arrive_expect_tx(&bars->k_full, C::kTileBytes);
+    for (int c = 0; c < C::kChunks; ++c)
+      tma_load_4d(smem + C::kKOff + c * C::kChunkBytes, tm_k, &bars->k_full, c * 64, t.kvh,
+                  t.br.n_start + j * kBN, t.b);
+    k_issued = g + 1;
+    if (bars->abort_flag) return false;
+  }
+  return true;
+}
+
+// V loads of one item (the V thread).
+__device__ bool tma_v256(const CUtensorMap *tm_v, uint8_t *smem, Bars256 *bars, const Work &t, int g0,
+                         int &v_issued) {
+  using C = Cfg256;
+  for (int j = 0; j < t.br.nb; ++j) {
+    const int g = g0 + j;
+    if (!mbar_wait_or_abort(&bars->v_empty, (g & 1) ^ 1, kTimeoutNs, &bars->abort_flag)) return false;
+    mbar_arrive_expect_tx(&bars->v_full, C::kTileBytes);
+    for (int c = 0; c < C::kChunks; ++c)
+      tma_load_4d(smem + C::kVOff + c * C::kChunkBytes, tm_v, &bars->v_full, c * 64, t.kvh,
+                  t.br.n_start + j * kBN, t.b);
+    v_issued = g + 1;
+    if (bars->abort_flag) return false;
+  }
+  return true;
+}
+
+// MMAs of one item: QK(g0), QK(g0 + 1), then per block PV(g), QK(g + 2).
+// Block g's scores live in S_(g & 1); s_full / p_full of a buffer complete
+// once per block that uses it (phase g >> 1); o_done once per block.
+template <bool kBF16, bool kFold>
+__device__ bool mma_256(uint8_t *smem, Bars256 *bars, uint32_t tmem, int nb, int tile_it, int g0) {
+  using C = Cfg256;
+  constexpr int D = C::D;
+  constexpr uint32_t idesc_qk = idesc_f16(128, kBN, kBF16, false);
+  constexpr uint32_t idesc_pv = idesc_f16(128, D, kBF16, true);
+  const uint32_t q_base = smem_u32(smem + C::kQOff);
+  const uint32_t k_base = smem_u32(smem + C::kKOff);
+  const uint32_t v_base = smem_u32(smem + C::kVOff);
+  const uint32_t x_base = smem_u32(smem + C::kXOff);
+  auto wait = [&](uint64_t *bar, uint32_t par) {
+    return mbar_wait_or_abort(bar, par, kTimeoutNs, &bars->abort_flag);
+  };
+  auto issue_qk = [&](int buf) {
+    const uint32_t d_tmem = tmem + (buf ? C::kTmemS1 : C::kTmemS0);
+    uint64_t da = smem_desc_sw128(q_base, 16, 1024);
+    uint64_t db = smem_desc_sw128(k_base, 16, 1024);
+    asm volatile("" : "+l"(da), "+l"(db));
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const uint64_t off = (uint64_t)(((kk / 4) * C::kChunkBytes + (kk % 4) * 32) >> 4);
+      mma_ss(d_tmem, da + off, db + off, idesc_qk, kk > 0 ? 1u : 0u);
+    }
+    if constexpr (kFold) {
+      uint64_t dx = smem_desc_noswz(x_base, 128, 256);
+      uint64_t dk = smem_desc_noswz(x_base + C::kXBytes, 128, 256);
+      asm volatile("" : "+l"(dx), "+l"(dk));
+      mma_ss(d_tmem, dx, dk, idesc_qk, 1u);
+    }
+  };
+  auto issue_pv = [&](int buf, bool acc) {
+    const uint32_t d_tmem = tmem + C::kTmemO;
+    const uint32_t p_tmem = tmem + (buf ? C::kTmemS1 : C::kTmemS0);
+    uint64_t db = smem_desc_sw128(v_base, C::kChunkBytes, 1024);
+    asm volatile("" : "+l"(db));
+#pragma unroll
+    for (int kk = 0; kk < kBN / 16; ++kk)
+      mma_ts(d_tmem, p_tmem + kk * 8, db + (uint64_t)((kk * 16 * 128) >> 4), idesc_pv, (acc || kk > 0) ? 1u : 0u);
+  };
+  // QK^T of block g (its K is in the single K slot).
+  auto qk_block = [&](int g, bool last) {
+    if (!wait(&bars->k_full, g & 1)) return false;
+    tc_fence_after();
+    issue_qk(g & 1);
+    tc_commit(&bars->s_full[g & 1]);
+    tc_commit(&bars->k_empty);
+    if (last) tc_commit(&bars->q_empty);
+    return true;
+  };
+  if (!wait(&bars->q_full, tile_it & 1)) return false;
+  if (!qk_block(g0, nb == 1)) return false;
+  if (nb > 1 && !qk_block(g0 + 1, nb == 2)) return false;
+  for (int j = 0; j < nb; ++j) {
+    const int g = g0 + j;
+    if (!wait(&bars->v_full, g & 1) || !wait(&bars->p_full[g & 1], (g >> 1) & 1)) return false;
+    tc_fence_after();
+    issue_pv(g & 1, j > 0);
+    tc_commit(&bars->o_done);
+    tc_commit(&bars->v_empty);
+    if (j + 2 < nb && !qk_block(g + 2, j + 3 == nb)) return false;
+    if (bars->abort_flag) return false;
+  }
+  return true;
+}
+
+// Softmax of one item (warps 0-3, thread r = row r = TMEM lane r), then the
+// epilogue.  g0: key blocks of earlier items.
+template <typename T, bool kAlibi, bool kSoftcap>
+__device__ bool softmax_256(const AttnArgs &a, Bars256 *bars, uint32_t tmem, int warp, const Work &w, int g0) {
+  using C = Cfg256;
+  constexpr int D = C::D;
+  const float kNegInf = -CUDART_INF_F;
+  const BlockRange br = w.br;
+  const int m0 = w.m0, h = w.h, b = w.b, ql = w.ql, kl = w.kl;
+  const int r = threadIdx.x;  // warps 0-3
+  const int qi = m0 + r;
+  const int off = diag_shift(a, ql, kl);
+  const int diag = qi + off;
+  const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
+  const uint32_t tO = tmem + lane_off + C::kTmemO;
+  const float scale2 = a.sm_scale * kLog2e;
+  const float slope2 = kAlibi ? a.alibi[h] * kLog2e : 0.f;
+  const float cap_in = kSoftcap ? a.sm_scale / a.softcap : 0.f;
+  const float cap_out = kSoftcap ? a.softcap * kLog2e : 0.f;
+  float m_used = kNegInf, l = 0.f;
+  bool aborted = false;
+
+  for (int j = 0; j < br.nb; ++j) {
+    const int g = g0 + j;
+    const int n0 = br.n_start + j * kBN;
+    const uint32_t tS = tmem + lane_off + ((g & 1) ? C::kTmemS1 : C::kTmemS0);
+    bool ok = mbar_wait_or_abort(&bars->s_full[g & 1], (g >> 1) & 1, kTimeoutNs, &bars->abort_flag);
+    if (!__all_sync(0xffffffffu, ok)) {
+      set_abort(bars, a.err);
+      aborted = true;
+      break;
+    }
+    tc_fence_after();
+    int lo = 0, hi = kBN;
+    const bool need_mask = (n0 + kBN > kl) || (a.causal && n0 + kBN - 1 > m0 + off) ||
+                           (a.window >= 0 && m0 + kBM - 1 + off - n0 > a.window);
+    if (need_mask) {
+      hi = min(kBN, kl - n0);
+      if (a.causal) hi = min(hi, diag - n0 + 1);
+      if (a.window >= 0) lo = max(0, diag - a.window - n0);
+    }
+    float alpha = 1.f;
+    bool rescale = false;
+    if (need_mask && __all_sync(0xffffffffu, hi <= lo)) {
+      uint32_t z[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) z[c] = 0u;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tmem_st16(tS + q * 16, z);
+    } else if (need_mask) {
+      softmax_block<T, kAlibi, kSoftcap, true>(tS, n0, a.kv_offset, lo, hi, scale2, slope2, cap_in, cap_out, m_used,
+                                               l, alpha, rescale);
+    } else {
+      softmax_block<T, kAlibi, kSoftcap, false>(tS, n0, a.kv_offset, lo, hi, scale2, slope2, cap_in, cap_out, m_used,
+                                                l, alpha, rescale);
+    }
+    if (__any_sync(0xffffffffu, rescale)) {
+      // O holds blocks 0..j-1 once PV(g - 1) is done; rescale it in place.
+      // (S(g) arriving means PV(g - 2) completed, so o_done is at most one
+      // phase behind the one waited for.)
+      ok = mbar_wait_or_abort(&bars->o_done, (g - 1) & 1, kTimeoutNs, &bars->abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        set_abort(bars, a.err);
+        aborted = true;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int ch = 0; ch < D / 32; ++ch) {
+        uint32_t o[32];
+        tmem_ld32(tO + ch * 32, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+        tmem_st32(tO + ch * 32, o);
+      }
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(&bars->p_full[g & 1]);
+  }
+
+  if (!aborted && br.nb > 0) {
+    // QK(g) is issued before PV(g - 1), so when the last block's scores
+    // arrived only PV(last - 2) was known complete: wait for o_done's phase
+    // last - 1 and then last (a parity wait must never be two phases ahead
+    // of the barrier, or it would match the older phase of equal parity).
+    const int gl = g0 + br.nb - 1;
+    bool ok = true;
+    if (br.nb >= 2) ok = mbar_wait_or_abort(&bars->o_done, (gl - 1) & 1, kTimeoutNs, &bars->abort_flag);
+    ok = ok && mbar_wait_or_abort(&bars->o_done, gl & 1, kTimeoutNs, &bars->abort_flag);
+    if (!__all_sync(0xffffffffu, ok)) {
+      set_abort(bars, a.err);
+      aborted = true;
+    } else {
+      tc_fence_after();
+    }
+  }
+  const bool have = !aborted && br.nb > 0;
+  const bool valid = qi < ql && l > 0.f;
+  const float inv = valid ? 1.f / l : 0.f;
+  const int gi = threadIdx.x & 3;
+  const int qi_group = qi - gi;
+  T *const obase = static_cast<T *>(a.o) + b * a.os[0] + h * a.os[2];
+#pragma unroll 1
+  for (int ch = 0; ch < D / 32; ++ch) {
+    uint32_t o[32];
+    if (have) {
+      tmem_ld32(tO + ch * 32, o);
+      tmem_wait_ld();
+      reg_fence32(o);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) o[c] = 0u;
+    }
+    uint32_t wv[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      wv[c] = valid ? pack2<T>(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv) : 0u;
+    uint4 u[4];
+#pragma unroll
+    for (int v4 = 0; v4 < 4; ++v4) u[v4] = make_uint4(wv[4 * v4], wv[4 * v4 + 1], wv[4 * v4 + 2], wv[4 * v4 + 3]);
+    transpose_units4(u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int row = qi_group + k;
+      if (row < a.Sq) *reinterpret_cast<uint4 *>(obase + (long long)row * a.os[1] + ch * 32 + gi * 8) = u[k];
+    }
+  }
+  if (a.lse != nullptr && qi < a.Sq)
+    a.lse[((long long)b * a.H + h) * a.Sq + qi] = valid ? (m_used + log2f(l)) * kLn2 : kNegInf;
+  return !aborted;
+}
+
+template <typename T, bool kAlibi, bool kSoftcap>
+__global__ void __launch_bounds__(kThreads256, 1)
+    fmha_sm100_d256_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                           const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int n_mblocks,
+                           const int group_units, const int n_work, int *work_ctr) {
+  using C = Cfg256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars256 *bars = reinterpret_cast<Bars256 *>(smem + C::kBarOff);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr bool kFold = kAlibi && !kSoftcap;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_empty, 1);
+    mbar_init(&bars->k_full, 1);
+    mbar_init(&bars->k_empty, 1);
+    mbar_init(&bars->v_full, 1);
+    mbar_init(&bars->v_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_full[i], kBM);
+    }
+    mbar_init(&bars->o_done, 1);
+    for (int i = 0; i < kSchedSlots; ++i) {
+      mbar_init(&bars->sched_full[i], 1);
+      mbar_init(&bars->sched_empty[i], kSchedConsumers256);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if constexpr (kFold) {
+    // B' row c = [c, c, c, 0, ...]; A' zero (its columns 0-2 are written per item).
+    for (int u = threadIdx.x; u < 2 * 256; u += kThreads256) {
+      const int op = u >> 8, e = u & 255;
+      const int r = (e >> 4) * 8 + (e & 7), khalf = (e >> 3) & 1;
+      const float c = (op == 1 && khalf == 0) ? (float)r : 0.f;
+      const float f[8] = {c, c, c, 0.f, 0.f, 0.f, 0.f, 0.f};
+      *reinterpret_cast<uint4 *>(smem + C::kXOff + op * C::kXBytes + x_offset(r, khalf * 8)) = pack8<T>(f);
+    }
+    fence_proxy_async_smem();
+  }
+  if (warp == kKWarp256 && lane == 0) {
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  if (warp == kMmaWarp256) {
+    tmem_alloc(&bars->tmem_base, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == kKWarp256 && lane == 0) {
+    int g = 0, it = 0, k_issued = 0, q_issued = 0;
+    int w = (int)blockIdx.x;
+    for (int seq = 0;; ++seq) {
+      if (!sched_publish(bars, seq, w)) {
+        set_abort(bars, a.err);
+        break;
+      }
+      if (w >= n_work) break;
+      const Work t = decode_work(a, w, n_mblocks, group_units, kBM);
+      if (t.br.nb > 0) {
+        uint4 beta = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (kFold) {
+          const float bb = a.alibi[t.h] / a.sm_scale;
+          const float r1 = bb - Elem<T>::to_f(Elem<T>::from_f(bb));
+          const float r2 = r1 - Elem<T>::to_f(Elem<T>::from_f(r1));
+          const float f[8] = {bb, r1, r2, 0.f, 0.f, 0.f, 0.f, 0.f};
+          beta = pack8<T>(f);
+        }
+        const bool ok = tma_k256<kFold>(&tm_q, &tm_k, smem, bars, t, it, g, k_issued, q_issued, beta);
+        g += t.br.nb;
+        ++it;
+        if (!ok) {
+          set_abort(bars, a.err);
+          break;
+        }
+      }
+      w = work_ctr != nullptr ? (int)gridDim.x + atomicAdd(work_ctr, 1) : n_work;
+    }
+    // Drain: every issued load lands before the CTA exits.
+    if (q_issued > 0) mbar_wait(&bars->q_full, (q_issued - 1) & 1, kTimeoutNs);
+    if (k_issued > 0) mbar_wait(&bars->k_full, (k_issued - 1) & 1, kTimeoutNs);
+  } else if (warp == kVWarp256 && lane == 0) {
+    int g = 0, v_issued = 0;
+    for (int seq = 0;; ++seq) {
+      const int w = sched_take(bars, seq, false);
+      if (w < 0) {
+        set_abort(bars, a.err);
+        break;
+      }
+      if (w >= n_work) break;
+      const Work t = decode_work(a, w, n_mblocks, group_units, kBM);
+      if (t.br.nb == 0) continue;
+      const bool ok = tma_v256(&tm_v, smem, bars, t, g, v_issued);
+      g += t.br.nb;
+      if (!ok) {
+        set_abort(bars, a.err);
+        break;
+      }
+    }
+    if (v_issued > 0) mbar_wait(&bars->v_full, (v_issued - 1) & 1, kTimeoutNs);
+  } else if (warp == kMmaWarp256 && lane == 0) {
+    int g = 0, it = 0;
+    for (int seq = 0;; ++seq) {
+      const int w = sched_take(bars, seq, false);
+      if (w < 0) {
+        set_abort(bars, a.err);
+        break;
+      }
+      if (w >= n_work) break;
+      const Work t = decode_work(a, w, n_mblocks, group_units, kBM);
+      if (t.br.nb == 0) continue;
+      const bool ok = mma_256<kBF16, kFold>(smem, bars, tmem, t.br.nb, it, g);
+      g += t.br.nb;
+      ++it;
+      if (!ok) {
+        set_abort(bars, a.err);
+        break;
+      }
+    }
+    tc_commit(&bars->drain);
+    mbar_wait(&bars->drain, 0, kTimeoutNs);
+  } else if (warp < 4) {
+    int g = 0;
+    for (int seq = 0;; ++seq) {
+      const int w = sched_take(bars, seq, true);
+      if (w < 0) {
+        set_abort(bars, a.err);
+        break;
+      }
+      if (w >= n_work) break;
+      const Work t = decode_work(a, w, n_mblocks, group_units, kBM);
+      if (!softmax_256<T, kAlibi, kSoftcap>(a, bars, tmem, warp, t, g)) break;
+      g += t.br.nb;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp256) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
 // -------------------------------------------------------------------- host
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
@@ -974,6 +1425,36 @@ bool make_tile_map(CUtensorMap *m, const void *base, bool bf16, int D, int S, in
   return r == CUDA_SUCCESS;
 }
 
+// Work-item geometry and grid of one launch: items of `rows` query rows per
+// (batch, head) unit, units grouped so a group's K/V (Skv * D * 4 bytes per
+// unit) stays within about half of the 126 MB L2; with a work counter one CTA
+// per SM (counter zeroed on the stream), else one CTA per item.
+struct LaunchShape {
+  int n_mblocks, group_units, n_work, grid;
+  int *ctr;
+};
+
+cudaError_t launch_shape(const AttnArgs &a, int D, int rows, int *work_ctr, cudaStream_t s, LaunchShape *out) {
+  const long long n_mblocks = (a.Sq + rows - 1) / rows;
+  const long long units = (long long)a.B * a.H;
+  // Item indices, and the counter's final values (up to n_work + 2 * grid), stay in int.
+  if (n_mblocks * units > 0x7fffffffLL - (1 << 20)) return cudaErrorInvalidValue;
+  const long long kv_unit = std::max<long long>(1, (long long)a.Skv * D * 4);
+  out->group_units = (int)std::max<long long>(1, std::min<long long>(units, (64ll << 20) / kv_unit));
+  out->n_mblocks = (int)n_mblocks;
+  out->n_work = (int)(n_mblocks * units);
+  const int sms = std::max(1, a.num_sms);
+  out->grid = out->n_work;
+  out->ctr = nullptr;
+  if (work_ctr != nullptr && out->n_work > sms) {
+    cudaError_t e = cudaMemsetAsync(work_ctr, 0, sizeof(int), s);
+    if (e != cudaSuccess) return e;
+    out->grid = sms;
+    out->ctr = work_ctr;
+  }
+  return cudaSuccess;
+}
+
 template <typename T, int D, bool kAlibi, bool kSoftcap>
 cudaError_t launch_t(const AttnArgs &a, int *work_ctr, cudaStream_t s) {
   using C = Cfg<D>;
@@ -990,40 +1471,53 @@ cudaError_t launch_t(const AttnArgs &a, int *work_ctr, cudaStream_t s) {
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   });
   if (attr_err != cudaSuccess) return attr_err;
-  const long long n_mblocks = (a.Sq + kTiles * kBM - 1) / (kTiles * kBM);
-  const long long units = (long long)a.B * a.H;
-  // Item indices, and the counter's final values (up to n_work + 2 * grid), stay in int.
-  if (n_mblocks * units > 0x7fffffffLL - (1 << 20)) return cudaErrorInvalidValue;
-  // Units per group: K and V rows of one unit take Skv * D * 4 bytes; keep a
-  // group's K/V within about half of the 126 MB L2.
-  const long long kv_unit = std::max<long long>(1, (long long)a.Skv * D * 4);
-  const int group_units = (int)std::max<long long>(1, std::min<long long>(units, (64ll << 20) / kv_unit));
-  const long long n_work = n_mblocks * units;
-  const int sms = std::max(1, a.num_sms);
-  int grid = (int)n_work;
-  if (work_ctr != nullptr && n_work > sms) {
-    cudaError_t e = cudaMemsetAsync(work_ctr, 0, sizeof(int), s);
-    if (e != cudaSuccess) return e;
-    grid = sms;
-  } else {
-    work_ctr = nullptr;
-  }
-  kern<<<grid, kThreads, C::kSmemBytes, s>>>(tq, tk, tv, a, (int)n_mblocks, group_units, (int)n_work, work_ctr);
+  LaunchShape ls;
+  cudaError_t e = launch_shape(a, D, kTiles * kBM, work_ctr, s, &ls);
+  if (e != cudaSuccess) return e;
+  kern<<<ls.grid, kThreads, C::kSmemBytes, s>>>(tq, tk, tv, a, ls.n_mblocks, ls.group_units, ls.n_work, ls.ctr);
+  return cudaGetLastError();
+}
+
+template <typename T, bool kAlibi, bool kSoftcap>
+cudaError_t launch_t256(const AttnArgs &a, int *work_ctr, cudaStream_t s) {
+  using C = Cfg256;
+  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  CUtensorMap tq, tk, tv;
+  if (!make_tile_map(&tq, a.q, bf16, C::D, a.Sq, a.H, a.B, a.qs) ||
+      !make_tile_map(&tk, a.k, bf16, C::D, a.Skv, a.Hkv, a.B, a.ks) ||
+      !make_tile_map(&tv, a.v, bf16, C::D, a.Skv, a.Hkv, a.B, a.vs))
+    return cudaErrorInvalidValue;
+  auto kern = fmha_sm100_d256_kernel<T, kAlibi, kSoftcap>;
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  LaunchShape ls;
+  cudaError_t e = launch_shape(a, C::D, kBM, work_ctr, s, &ls);
+  if (e != cudaSuccess) return e;
+  kern<<<ls.grid, kThreads256, C::kSmemBytes, s>>>(tq, tk, tv, a, ls.n_mblocks, ls.group_units, ls.n_work, ls.ctr);
   return cudaGetLastError();
 }
 
 template <typename T, int D>
 cudaError_t launch_d(const AttnArgs &a, int *ctr, cudaStream_t s) {
   const bool alibi = a.alibi != nullptr, cap = a.softcap > 0.f;
-  if (alibi) return cap ? launch_t<T, D, true, true>(a, ctr, s) : launch_t<T, D, true, false>(a, ctr, s);
-  return cap ? launch_t<T, D, false, true>(a, ctr, s) : launch_t<T, D, false, false>(a, ctr, s);
+  if constexpr (D == 256) {
+    if (alibi) return cap ? launch_t256<T, true, true>(a, ctr, s) : launch_t256<T, true, false>(a, ctr, s);
+    return cap ? launch_t256<T, false, true>(a, ctr, s) : launch_t256<T, false, false>(a, ctr, s);
+  } else {
+    if (alibi) return cap ? launch_t<T, D, true, true>(a, ctr, s) : launch_t<T, D, true, false>(a, ctr, s);
+    return cap ? launch_t<T, D, false, true>(a, ctr, s) : launch_t<T, D, false, false>(a, ctr, s);
+  }
 }
 
 }  // namespace
 
 bool sm100_supports(const AttnArgs &a) {
   if (a.dtype != 1 && a.dtype != 2) return false;
-  if (a.D != 64 && a.D != 128) return false;
+  if (a.D != 64 && a.D != 128 && a.D != 256) return false;
   // The softmax takes the row max on raw scores, which needs an increasing
   // score transform (sm_scale > 0); other scales run on the SIMT kernel.
   if (!(a.sm_scale > 0.f)) return false;
@@ -1041,7 +1535,11 @@ cudaError_t launch_sm100(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStrea
   int *ctr = (ws != nullptr && ws_bytes >= sizeof(int) && (reinterpret_cast<uintptr_t>(ws) & 3u) == 0)
                  ? static_cast<int *>(ws)
                  : nullptr;
-  if (a.dtype == 1) return a.D == 64 ? launch_d<__half, 64>(a, ctr, s) : launch_d<__half, 128>(a, ctr, s);
+  if (a.dtype == 1) {
+    if (a.D == 256) return launch_d<__half, 256>(a, ctr, s);
+    return a.D == 64 ? launch_d<__half, 64>(a, ctr, s) : launch_d<__half, 128>(a, ctr, s);
+  }
+  if (a.D == 256) return launch_d<__nv_bfloat16, 256>(a, ctr, s);
   return a.D == 64 ? launch_d<__nv_bfloat16, 64>(a, ctr, s) : launch_d<__nv_bfloat16, 128>(a, ctr, s);
 }
 

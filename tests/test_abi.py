@@ -82,6 +82,10 @@ def _params(**over):
     return p
 
 
+def lib_ok(p):
+    return _lib.load().llmx_attn_set_contiguous_strides(ctypes.byref(p)) == 0
+
+
 def _select(p):
     out = ctypes.c_int32(-1)
     st = _lib.load().llmx_attn_select_algo(ctypes.byref(p), ctypes.byref(out))
@@ -119,6 +123,9 @@ def test_algorithm_selection():
     assert _select(_params(max_q_len=1)) == (0, _lib.ALGO["decode"])
     assert _select(_params(dtype=0)) == (0, _lib.ALGO["simt"])
     assert _select(_params(head_dim=80)) == (0, _lib.ALGO["simt"])
+    # head_dim 256 prefill runs on the tensor-core kernel (one query tile per work item)
+    p256 = _params(head_dim=256)
+    assert lib_ok(p256) and _select(p256) == (0, _lib.ALGO["tcgen05"])
     # unaligned base pointer: vector/TMA paths refuse, SIMT takes it
     assert _select(_params(q=0x10002)) == (0, _lib.ALGO["simt"])
     # forcing a path that cannot run the request is an error, not a fallback
