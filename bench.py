@@ -40,7 +40,7 @@ sys.path.insert(0, ROOT)
 
 HEADLINE = "llama7b_prefill_bf16_b8_h32_s2048_d128"
 EXTRA = ["padded_prefill_fp16_b4_h16_s1024_d64", "bloom_decode_bf16_b64_h32_kv4096_d128",
-         "long_prefill_bf16_b1_h32_s32768_d128", "cpu_fp32_b1_h8_s128_d64"]
+         "long_prefill_bf16_b1_h32_s32768_d128", "cpu_fp32_b1_h8_s128_d64", "gemma_prefill_bf16_b2_h16_s4096_d256"]
 L2_FLUSH_BYTES = 256 << 20
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 

@@ -1,4 +1,5 @@
-"""The five attention workloads this engine is measured on, with their
+"""The attention workloads this engine is measured on (five configurations
+of the reference's use cases plus a head_dim 256 prefill), with their
 seeded synthetic inputs and algorithmic work counts.
 
 Recipe (shared by the tests and the benchmark): a CPU ``torch.Generator``
@@ -68,6 +69,10 @@ WORKLOADS = {
         "BLOOM-style batched decode: B64 H32 Sq1 KV<=4096 D128 bf16, ALiBi, padded cache",
         torch.bfloat16, 64, 32, 32, 1, 4096, 128, causal=True, alibi=True, lens=(256, 4097),
         device_inputs=True),
+    "gemma_prefill_bf16_b2_h16_s4096_d256": Workload(
+        "gemma_prefill_bf16_b2_h16_s4096_d256",
+        "Head-dim-256 causal prefill (Gemma-7B-shaped heads): B2 H16 S4096 D256 bf16",
+        torch.bfloat16, 2, 16, 16, 4096, 4096, 256, causal=True, alibi=False, device_inputs=True),
     "long_prefill_bf16_b1_h32_s32768_d128": Workload(
         "long_prefill_bf16_b1_h32_s32768_d128",
         "Long-context causal prefill: B1 H32 S32768 D128 bf16, ALiBi",
