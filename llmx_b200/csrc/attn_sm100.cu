@@ -27,7 +27,8 @@
 //   O0 += P0(j) V(j),   S0(j+1) = Q0 K(j+1)^T,   O1 += P1(j) V(j),   S1(j+1)
 // so each softmax warpgroup's exponentials overlap the other tile's GEMMs;
 // tcgen05 operations from one thread execute in issue order, which is what
-// lets S0(j+1) overwrite P0(j) right after PV0(j) is issued.
+// lets S0(j+1) overwrite P0(j) right after PV0(j) is issued.  With ALiBi the
+// key blocks are taken last to first (block_n0), as in the reference.
 //
 // Online softmax: running max m and sum l per row in log2 units.  The max is
 // only moved (and O rescaled in tensor memory) when a block raises it by more
@@ -131,6 +132,16 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 struct BlockRange {
   int n_start, nb;
 };
+
+// First key of the j-th block processed.  With ALiBi the blocks go last to
+// first, as the reference's main loop does (single_mha_kernel.cuh:295-296):
+// the bias slope * key grows with the key, so the first block processed
+// holds the row's largest biases, the running max is set there, and later
+// blocks rarely raise it (each raise rescales O).
+template <bool kReverse>
+__device__ __forceinline__ int block_n0(const BlockRange &br, int j) {
+  return br.n_start + (kReverse ? br.nb - 1 - j : j) * kBN;
+}
 
 // rows: query rows per work item (kTiles * kBM, or kBM for head_dim 256).
 __device__ __forceinline__ BlockRange block_range(const AttnArgs &a, int m0, int ql, int kl, int rows) {
@@ -246,7 +257,7 @@ struct TmaCounts {
 // once the previous item's last QK^T on it has completed (q_empty).
 // With kFold the thread also writes the item's ALiBi row (beta: the slope
 // over sm_scale as three 16-bit parts) into A'_q before signalling Q_q.
-template <int D, bool kFold>
+template <int D, bool kFold, bool kReverse>
 __device__ bool tma_tile(const CUtensorMap *tm_q, const CUtensorMap *tm_k, const CUtensorMap *tm_v, uint8_t *smem,
                          Bars *bars, const Work &t, int tile_it, int kv_base, TmaCounts &n, uint4 beta) {
   using C = Cfg<D>;
@@ -273,7 +284,7 @@ __device__ bool tma_tile(const CUtensorMap *tm_q, const CUtensorMap *tm_k, const
     const int g = kv_base + j;
     const int s = g % C::kStages;
     const uint32_t par = ((g / C::kStages) & 1) ^ 1;
-    const int n0 = t.br.n_start + j * kBN;
+    const int n0 = block_n0<kReverse>(t.br, j);
     if (!wait(&bars->k_empty[s], par)) return false;
     mbar_arrive_expect_tx(&bars->k_full[s], C::kTileBytes);
     for (int c = 0; c < C::kChunks; ++c)
@@ -309,9 +320,13 @@ __device__ void tma_drain(Bars *bars, const TmaCounts &n) {
 // MMAs of one work item.  kv_base: key blocks of earlier items (ring
 // position); blk_base0 / blk_base1: key blocks of earlier items on tile 0 /
 // tile 1 (s_full, p_full, o_done complete once per block of their tile);
-// tile_it: earlier items (q_full phase).  The last QK^T on each Q buffer is followed by a commit to
-// q_empty, so the next item's Q load starts while this item finishes.
-template <int D, bool kBF16, bool kFold>
+// tile_it: earlier items (q_full phase).  The last QK^T on each Q buffer is
+// followed by a commit to q_empty, so the next item's Q load starts while
+// this item finishes.  Tile 1 takes part in all nb blocks; tile 0 (the
+// earlier rows) in nb0 of them: the first nb0 in forward order, the last
+// nb0 in reverse order (kReverse: the key blocks go last to first, so tile
+// 0's blocks, the lowest keys, come at the end).
+template <int D, bool kBF16, bool kFold, bool kReverse>
 __device__ bool mma_tile(uint8_t *smem, Bars *bars, uint32_t tmem, int nb, int nb0, int tile_it, int kv_base,
                          int blk_base0, int blk_base1) {
   using C = Cfg<D>;
@@ -360,38 +375,44 @@ __device__ bool mma_tile(uint8_t *smem, Bars *bars, uint32_t tmem, int nb, int n
       mma_ts(d_tmem, p_tmem + kk * 8, db + (uint64_t)((kk * 16 * 128) >> 4), idesc_pv, (acc || kk > 0) ? 1u : 0u);
   };
 
+  // Tile 0 works on blocks j in [lo0, hi0) of the item's sequence.
+  const int lo0 = kReverse ? nb - nb0 : 0, hi0 = kReverse ? nb : nb0;
   const uint32_t qpar = tile_it & 1;
   const int s0 = kv_base % C::kStages;
-  if (!wait(&bars->q_full[0], qpar) || !wait(&bars->k_full[s0], (kv_base / C::kStages) & 1)) return false;
-  tc_fence_after();
-  issue_qk(0, s0);
-  tc_commit(&bars->s_full[0]);
-  if (nb0 == 1) tc_commit(&bars->q_empty[0]);
+  if (!wait(&bars->k_full[s0], (kv_base / C::kStages) & 1)) return false;
+  if (lo0 == 0) {
+    if (!wait(&bars->q_full[0], qpar)) return false;
+    tc_fence_after();
+    issue_qk(0, s0);
+    tc_commit(&bars->s_full[0]);
+    if (hi0 == 1) tc_commit(&bars->q_empty[0]);
+  }
   if (!wait(&bars->q_full[1], qpar)) return false;
   tc_fence_after();
   issue_qk(1, s0);
   tc_commit(&bars->s_full[1]);
   tc_commit(&bars->k_empty[s0]);
   if (nb == 1) tc_commit(&bars->q_empty[1]);
-  // Tile 0 (the earlier rows) runs blocks [0, nb0), tile 1 all nb blocks.
   for (int j = 0; j < nb; ++j) {
     const int g = kv_base + j;
     const int sv = g % C::kStages;
     const int sk = (g + 1) % C::kStages;
     const bool more = j + 1 < nb;
     if (!wait(&bars->v_full[sv], (g / C::kStages) & 1)) return false;
-    if (j < nb0) {
-      if (!wait(&bars->p_full[0], (blk_base0 + j) & 1)) return false;
+    if (j >= lo0 && j < hi0) {
+      if (!wait(&bars->p_full[0], (blk_base0 + j - lo0) & 1)) return false;
       tc_fence_after();
-      issue_pv(0, sv, j > 0);
+      issue_pv(0, sv, j > lo0);
       tc_commit(&bars->o_done[0]);
     }
     if (more && !wait(&bars->k_full[sk], ((g + 1) / C::kStages) & 1)) return false;
-    if (j + 1 < nb0) {
+    if (j + 1 >= lo0 && j + 1 < hi0) {
+      // Tile 0's first block in reverse order: its Q load is awaited here.
+      if (j + 1 == lo0 && !wait(&bars->q_full[0], qpar)) return false;
       tc_fence_after();
       issue_qk(0, sk);
       tc_commit(&bars->s_full[0]);
-      if (j + 2 == nb0) tc_commit(&bars->q_empty[0]);
+      if (j + 2 == hi0) tc_commit(&bars->q_empty[0]);
     }
     if (!wait(&bars->p_full[1], (blk_base1 + j) & 1)) return false;
     tc_fence_after();
@@ -677,7 +698,7 @@ __device__ bool softmax_tile(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
   bool aborted = false;
 
   for (int j = 0; j < br.nb; ++j) {
-    const int n0 = br.n_start + j * kBN;
+    const int n0 = block_n0<kAlibi>(br, j);
     bool ok = mbar_wait_or_abort(&bars->s_full[t], (blk_base + j) & 1, kTimeoutNs, &bars->abort_flag);
     if (!__all_sync(0xffffffffu, ok)) {
       set_abort(bars, a.err);
@@ -875,7 +896,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float f[8] = {b, r1, r2, 0.f, 0.f, 0.f, 0.f, 0.f};
             beta = pack8<T>(f);
           }
-          const bool ok = tma_tile<D, kFold>(&tm_q, &tm_k, &tm_v, smem, bars, t, it, kv, n, beta);
+          const bool ok = tma_tile<D, kFold, kAlibi>(&tm_q, &tm_k, &tm_v, smem, bars, t, it, kv, n, beta);
           kv += t.br.nb;
           ++it;
           if (!ok) {
@@ -897,8 +918,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (w >= n_work) break;
         const Work t = decode_work(a, w, n_mblocks, group_units);
         if (t.br.nb == 0) continue;
-        const bool ok = mma_tile<D, std::is_same<T, __nv_bfloat16>::value, kFold>(smem, bars, tmem, t.br.nb, t.nb0,
-                                                                                    it, kv, blk0, kv);
+        const bool ok = mma_tile<D, std::is_same<T, __nv_bfloat16>::value, kFold, kAlibi>(smem, bars, tmem, t.br.nb,
+                                                                                            t.nb0, it, kv, blk0, kv);
         kv += t.br.nb;
         blk0 += t.nb0;
         ++it;
@@ -977,7 +998,7 @@ struct Bars256 {
 static_assert(sizeof(Bars256) <= 1024, "barrier region");
 
 // K / Q loads of one item (the K thread); g0: key blocks of earlier items.
-template <bool kFold>
+template <bool kFold, bool kReverse>
 __device__ bool tma_k256(const CUtensorMap *tm_q, const CUtensorMap *tm_k, uint8_t *smem, Bars256 *bars,
                          const Work &t, int tile_it, int g0, int &k_issued, int &q_issued, uint4 beta) {
   using C = Cfg256;
@@ -1001,7 +1022,7 @@ __device__ bool tma_k256(const CUtensorMap *tm_q, const CUtensorMap *tm_k, uint8
     mbar_arrive_expect_tx(&bars->k_full, C::kTileBytes);
     for (int c = 0; c < C::kChunks; ++c)
       tma_load_4d(smem + C::kKOff + c * C::kChunkBytes, tm_k, &bars->k_full, c * 64, t.kvh,
-                  t.br.n_start + j * kBN, t.b);
+                  block_n0<kReverse>(t.br, j), t.b);
     k_issued = g + 1;
     if (bars->abort_flag) return false;
   }
@@ -1009,6 +1030,7 @@ __device__ bool tma_k256(const CUtensorMap *tm_q, const CUtensorMap *tm_k, uint8
 }
 
 // V loads of one item (the V thread).
+template <bool kReverse>
 __device__ bool tma_v256(const CUtensorMap *tm_v, uint8_t *smem, Bars256 *bars, const Work &t, int g0,
                          int &v_issued) {
   using C = Cfg256;
@@ -1018,7 +1040,7 @@ __device__ bool tma_v256(const CUtensorMap *tm_v, uint8_t *smem, Bars256 *bars, 
     mbar_arrive_expect_tx(&bars->v_full, C::kTileBytes);
     for (int c = 0; c < C::kChunks; ++c)
       tma_load_4d(smem + C::kVOff + c * C::kChunkBytes, tm_v, &bars->v_full, c * 64, t.kvh,
-                  t.br.n_start + j * kBN, t.b);
+                  block_n0<kReverse>(t.br, j), t.b);
     v_issued = g + 1;
     if (bars->abort_flag) return false;
   }
@@ -1117,7 +1139,7 @@ __device__ bool softmax_256(const AttnArgs &a, Bars256 *bars, uint32_t tmem, int
 
   for (int j = 0; j < br.nb; ++j) {
     const int g = g0 + j;
-    const int n0 = br.n_start + j * kBN;
+    const int n0 = block_n0<kAlibi>(br, j);
     const uint32_t tS = tmem + lane_off + ((g & 1) ? C::kTmemS1 : C::kTmemS0);
     bool ok = mbar_wait_or_abort(&bars->s_full[g & 1], (g >> 1) & 1, kTimeoutNs, &bars->abort_flag);
     if (!__all_sync(0xffffffffu, ok)) {
@@ -1305,7 +1327,7 @@ __global__ void __launch_bounds__(kThreads256, 1)
           const float f[8] = {bb, r1, r2, 0.f, 0.f, 0.f, 0.f, 0.f};
           beta = pack8<T>(f);
         }
-        const bool ok = tma_k256<kFold>(&tm_q, &tm_k, smem, bars, t, it, g, k_issued, q_issued, beta);
+        const bool ok = tma_k256<kFold, kAlibi>(&tm_q, &tm_k, smem, bars, t, it, g, k_issued, q_issued, beta);
         g += t.br.nb;
         ++it;
         if (!ok) {
@@ -1329,7 +1351,7 @@ __global__ void __launch_bounds__(kThreads256, 1)
       if (w >= n_work) break;
       const Work t = decode_work(a, w, n_mblocks, group_units, kBM);
       if (t.br.nb == 0) continue;
-      const bool ok = tma_v256(&tm_v, smem, bars, t, g, v_issued);
+      const bool ok = tma_v256<kAlibi>(&tm_v, smem, bars, t, g, v_issued);
       g += t.br.nb;
       if (!ok) {
         set_abort(bars, a.err);
