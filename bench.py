@@ -287,8 +287,9 @@ def bench_workload(name, steps, warmup, rank, world, device, stream, peaks, with
 
 
 def bench_kv_split(steps, warmup, rank, world, device, stream, peaks):
-    """Long-context prefill with its keys split over all ranks (zig-zag chunks,
-    NCCL log-sum-exp merge); strong scaling: the job is one fixed sequence."""
+    """Long-context prefill with its keys split over all ranks
+    (parallel.kv_split_ranges, NCCL log-sum-exp merge); strong scaling: the
+    job is one fixed sequence."""
     import torch.distributed as dist
 
     from llmx_b200 import parallel
@@ -297,7 +298,7 @@ def bench_kv_split(steps, warmup, rank, world, device, stream, peaks):
     w = WORKLOADS["long_prefill_bf16_b1_h32_s32768_d128"]
     inp = make_inputs(w, device)
     S = w.q_len
-    chunks = parallel.zigzag_chunks(S, world, rank)
+    chunks = parallel.kv_split_ranges(S, world, rank)
     kc = [inp.k[:, a:b] for a, b in chunks]
     vc = [inp.v[:, a:b] for a, b in chunks]
     offs = [a for a, _ in chunks]

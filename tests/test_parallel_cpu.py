@@ -42,6 +42,39 @@ def test_zigzag_chunks_cover_once_and_balance_causal_work(S, world):
         assert max(work) / min(work) < 1.02
 
 
+@pytest.mark.parametrize("S,world", [(32768, 2), (32768, 4), (32768, 8), (131072, 8), (1000, 3), (100, 8)])
+def test_causal_key_range_covers_once_and_balances_causal_work(S, world):
+    ranges = [parallel.causal_key_range(S, world, r) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == S
+    for (a0, b0), (a1, b1) in zip(ranges, ranges[1:]):
+        assert a0 <= b0 == a1 <= b1
+    # visible causal pairs of all S queries over keys [a, b): sum of S - j
+    work = [(b - a) * S - (b * (b - 1) - a * (a - 1)) / 2 for a, b in ranges]
+    assert sum(work) == S * (S + 1) / 2
+    if S >= 32768:
+        assert max(work) / min(work) < 1.01
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_kv_split_ranges_cover_every_key_once(world):
+    S = 32768
+    covered = sorted(j for r in range(world) for a, b in parallel.kv_split_ranges(S, world, r) for j in range(a, b))
+    assert covered == list(range(S))
+
+
+def test_merge_of_causal_key_ranges_equals_full_attention():
+    g = torch.Generator().manual_seed(2)
+    S, H, D = 333, 2, 32
+    q, k, v = (torch.randn(1, S, H, D, generator=g) for _ in range(3))
+    a = oracle.alibi_slopes(H)
+    full, lfull = oracle.attention_ref(q[0], k[0], v[0], alibi=a, return_lse=True)
+    chunks = [parallel.causal_key_range(S, 4, r) for r in range(4)]
+    outs, lses = _partials(q, k, v, chunks, a, S)
+    out, lse = parallel.merge_partials(outs, lses)
+    torch.testing.assert_close(out[0], full, atol=2e-6, rtol=0)
+    torch.testing.assert_close(lse[0], lfull, atol=2e-6, rtol=0)
+
+
 def _partials(q, k, v, chunks, alibi, S):
     outs, lses = [], []
     for a, b in chunks:
