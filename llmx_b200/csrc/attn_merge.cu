@@ -14,14 +14,22 @@
 // Same running max / sum algebra as the reference's online softmax
 // (softmax.h:53-110), applied across shards instead of key blocks.
 //
-// Bandwidth-bound elementwise kernels: one warp per (b, s, h) row, 16-byte
-// vector accesses, every byte read or written once.
+// Bandwidth-bound elementwise kernels.  A block takes one (b, h) and a run of
+// rows_of(D) consecutive s: the per-row weights come from contiguous lse /
+// row-max entries ([B, H, S] layout) into shared memory once, then every
+// thread moves four 16-byte units of the rows' D elements (units of one row
+// are adjacent lanes, so each row's D contiguous elements are read in one
+// pass); all loads of a thread are issued before its arithmetic.  Every byte
+// is read or written once.
 #include "common.cuh"
 
 namespace llmx_b200 {
 namespace {
 
 constexpr int kMaxParts = 8;
+constexpr int kMergeThreads = 256;
+constexpr int kUnitsPerThread = 4;
+constexpr int kMaxRows = 128;
 
 struct MergeArgs {
   int n_parts, B, S, H, D, dtype;
@@ -34,88 +42,140 @@ struct MergeArgs {
   float *lse_out;                 // [B, H, S] or null
 };
 
-template <typename T>
-__global__ void __launch_bounds__(256) merge_scale_kernel(MergeArgs a) {
-  const long long row = (long long)blockIdx.x * 8 + threadIdx.x / 32;  // (b, s, h)
-  const int lane = threadIdx.x % 32;
-  const long long rows = (long long)a.B * a.S * a.H;
-  if (row >= rows) return;
-  const int h = (int)(row % a.H);
-  const long long bs = row / a.H;
-  const int s = (int)(bs % a.S), b = (int)(bs / a.S);
-  const long long li = ((long long)b * a.H + h) * a.S + s;
-  const float m = a.m[li];
-  const float m_safe = isinf(m) ? 0.f : m;
-  float w[kMaxParts];
-  float ws = 0.f;
-#pragma unroll
-  for (int c = 0; c < kMaxParts; ++c) {
-    w[c] = 0.f;
-    if (c < a.n_parts) {
-      const float l = a.lse[c][li];
-      w[c] = (l == -CUDART_INF_F) ? 0.f : expf(l - m_safe);
-      ws += w[c];
-    }
-  }
-  // D / 8 lanes of 8 elements each
-  for (int d0 = lane * 8; d0 < a.D; d0 += 32 * 8) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int c = 0; c < kMaxParts; ++c) {
-      if (c < a.n_parts && w[c] != 0.f) {
-        const T *src = static_cast<const T *>(a.o[c]) + row * a.D + d0;
-        float f[8];
-        unpack8<T>(*reinterpret_cast<const uint4 *>(src), f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = fmaf(w[c], f[e], acc[e]);
-      }
-    }
-    float4 *dst = reinterpret_cast<float4 *>(a.num + row * a.D + d0);
-    dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-  }
-  if (lane == 0) a.wsum[li] = ws;
+// Rows per block: enough for kUnitsPerThread 8-element units per thread.
+__host__ __device__ inline int rows_of(int D) {
+  const int r = kMergeThreads * kUnitsPerThread / (D / 8);
+  return r < 1 ? 1 : (r > kMaxRows ? kMaxRows : r);
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) merge_finish_kernel(MergeArgs a) {
-  const long long row = (long long)blockIdx.x * 8 + threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
-  const long long rows = (long long)a.B * a.S * a.H;
-  if (row >= rows) return;
-  const int h = (int)(row % a.H);
-  const long long bs = row / a.H;
-  const int s = (int)(bs % a.S), b = (int)(bs / a.S);
-  const long long li = ((long long)b * a.H + h) * a.S + s;
-  const float ws = a.wsum[li];
-  const float inv = ws > 0.f ? 1.f / ws : 0.f;
-  for (int d0 = lane * 8; d0 < a.D; d0 += 32 * 8) {
-    const float4 *src = reinterpret_cast<const float4 *>(a.num + row * a.D + d0);
-    const float4 x = src[0], y = src[1];
-    const float f[8] = {x.x * inv, x.y * inv, x.z * inv, x.w * inv, y.x * inv, y.y * inv, y.z * inv, y.w * inv};
-    *reinterpret_cast<uint4 *>(static_cast<T *>(a.out) + row * a.D + d0) = pack8<T>(f);
+__global__ void __launch_bounds__(kMergeThreads) merge_scale_kernel(MergeArgs a) {
+  __shared__ float w_s[kMaxParts][kMaxRows];
+  const int R = rows_of(a.D), V = a.D / 8;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int s0 = blockIdx.x * R;
+  const long long lrow = ((long long)b * a.H + h) * a.S;  // [B, H, S] row base
+  for (int r = threadIdx.x; r < R; r += kMergeThreads) {
+    const int s = s0 + r;
+    if (s >= a.S) break;
+    const float m = a.m[lrow + s];
+    const float m_safe = isinf(m) ? 0.f : m;
+    float ws = 0.f;
+    for (int c = 0; c < a.n_parts; ++c) {
+      const float l = a.lse[c][lrow + s];
+      const float w = (l == -CUDART_INF_F) ? 0.f : expf(l - m_safe);
+      w_s[c][r] = w;
+      ws += w;
+    }
+    a.wsum[lrow + s] = ws;
   }
-  if (lane == 0 && a.lse_out != nullptr) {
-    const float m = a.m[li];
-    a.lse_out[li] = ws > 0.f ? (isinf(m) ? 0.f : m) + logf(ws) : -CUDART_INF_F;
+  __syncthreads();
+  const int rows = min(R, a.S - s0);
+  const int n_units = rows * V;
+  // Per partial: the thread's four units loaded first, then accumulated.
+  float acc[kUnitsPerThread][8];
+#pragma unroll
+  for (int k = 0; k < kUnitsPerThread; ++k)
+#pragma unroll
+    for (int x = 0; x < 8; ++x) acc[k][x] = 0.f;
+  for (int c = 0; c < a.n_parts; ++c) {
+    const T *src = static_cast<const T *>(a.o[c]);
+    uint4 raw[kUnitsPerThread];
+#pragma unroll
+    for (int k = 0; k < kUnitsPerThread; ++k) {
+      const int idx = threadIdx.x + k * kMergeThreads;
+      raw[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (idx < n_units) {
+        const int r = idx / V, u = idx - r * V;
+        if (w_s[c][r] != 0.f)
+          raw[k] = *reinterpret_cast<const uint4 *>(src + (((long long)b * a.S + s0 + r) * a.H + h) * a.D + u * 8);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kUnitsPerThread; ++k) {
+      const int idx = threadIdx.x + k * kMergeThreads;
+      if (idx < n_units) {
+        const float w = w_s[c][idx / V];
+        float f[8];
+        unpack8<T>(raw[k], f);
+#pragma unroll
+        for (int x = 0; x < 8; ++x) acc[k][x] = fmaf(w, f[x], acc[k][x]);
+      }
+    }
   }
+#pragma unroll
+  for (int k = 0; k < kUnitsPerThread; ++k) {
+    const int idx = threadIdx.x + k * kMergeThreads;
+    if (idx >= n_units) break;
+    const int r = idx / V, u = idx - r * V;
+    float4 *dst = reinterpret_cast<float4 *>(a.num + (((long long)b * a.S + s0 + r) * a.H + h) * a.D + u * 8);
+    dst[0] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+    dst[1] = make_float4(acc[k][4], acc[k][5], acc[k][6], acc[k][7]);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kMergeThreads) merge_finish_kernel(MergeArgs a) {
+  __shared__ float inv_s[kMaxRows];
+  const int R = rows_of(a.D), V = a.D / 8;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int s0 = blockIdx.x * R;
+  const long long lrow = ((long long)b * a.H + h) * a.S;
+  for (int r = threadIdx.x; r < R; r += kMergeThreads) {
+    const int s = s0 + r;
+    if (s >= a.S) break;
+    const float ws = a.wsum[lrow + s];
+    inv_s[r] = ws > 0.f ? 1.f / ws : 0.f;
+    if (a.lse_out != nullptr) {
+      const float m = a.m[lrow + s];
+      a.lse_out[lrow + s] = ws > 0.f ? (isinf(m) ? 0.f : m) + logf(ws) : -CUDART_INF_F;
+    }
+  }
+  __syncthreads();
+  const int rows = min(R, a.S - s0);
+  const int n_units = rows * V;
+  float4 x[kUnitsPerThread][2];
+#pragma unroll
+  for (int k = 0; k < kUnitsPerThread; ++k) {
+    const int idx = threadIdx.x + k * kMergeThreads;
+    if (idx >= n_units) break;
+    const int r = idx / V, u = idx - r * V;
+    const long long e = (((long long)b * a.S + s0 + r) * a.H + h) * a.D + u * 8;
+    const float4 *src = reinterpret_cast<const float4 *>(a.num + e);
+    x[k][0] = src[0];
+    x[k][1] = src[1];
+  }
+#pragma unroll
+  for (int k = 0; k < kUnitsPerThread; ++k) {
+    const int idx = threadIdx.x + k * kMergeThreads;
+    if (idx >= n_units) break;
+    const int r = idx / V, u = idx - r * V;
+    const long long e = (((long long)b * a.S + s0 + r) * a.H + h) * a.D + u * 8;
+    const float inv = inv_s[r];
+    const float f[8] = {x[k][0].x * inv, x[k][0].y * inv, x[k][0].z * inv, x[k][0].w * inv,
+                        x[k][1].x * inv, x[k][1].y * inv, x[k][1].z * inv, x[k][1].w * inv};
+    *reinterpret_cast<uint4 *>(static_cast<T *>(a.out) + e) = pack8<T>(f);
+  }
+}
+
+dim3 merge_grid(const MergeArgs &a) {
+  const int R = rows_of(a.D);
+  return dim3((unsigned)((a.S + R - 1) / R), (unsigned)a.H, (unsigned)a.B);
 }
 
 cudaError_t launch_scale(const MergeArgs &a, cudaStream_t st) {
-  const unsigned blocks = (unsigned)(((long long)a.B * a.S * a.H + 7) / 8);
   if (a.dtype == LLMX_FP16)
-    merge_scale_kernel<__half><<<blocks, 256, 0, st>>>(a);
+    merge_scale_kernel<__half><<<merge_grid(a), kMergeThreads, 0, st>>>(a);
   else
-    merge_scale_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(a);
+    merge_scale_kernel<__nv_bfloat16><<<merge_grid(a), kMergeThreads, 0, st>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_finish(const MergeArgs &a, cudaStream_t st) {
-  const unsigned blocks = (unsigned)(((long long)a.B * a.S * a.H + 7) / 8);
   if (a.dtype == LLMX_FP16)
-    merge_finish_kernel<__half><<<blocks, 256, 0, st>>>(a);
+    merge_finish_kernel<__half><<<merge_grid(a), kMergeThreads, 0, st>>>(a);
   else
-    merge_finish_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(a);
+    merge_finish_kernel<__nv_bfloat16><<<merge_grid(a), kMergeThreads, 0, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -132,6 +192,9 @@ static llmx_status merge_common(MergeArgs *m, int32_t n_parts, const void *const
     return record_error(LLMX_ERR_UNSUPPORTED, "lse merge: dtype must be fp16 or bf16");
   if (B < 1 || S < 1 || H < 1 || D < 8 || D % 8)
     return record_error(LLMX_ERR_INVALID_ARGUMENT, "lse merge: B, S, H >= 1 and head_dim a multiple of 8");
+  if (B > 65535 || H > 65535 || D > 8192)
+    return record_error(LLMX_ERR_INVALID_ARGUMENT,
+                        "lse merge: batch and n_heads must be at most 65535, head_dim at most 8192");
   m->n_parts = n_parts;
   m->B = B;
   m->S = S;

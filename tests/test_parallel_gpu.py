@@ -104,16 +104,21 @@ def test_kv_split_two_gpus_nccl(tmp_path):
     assert (res["out"].float() - full.float().cpu()).abs().max().item() <= 2e-2
 
 
-@pytest.mark.parametrize("n_parts", [1, 2, 3, 8])
-def test_merge_kernels_match_torch_merge(n_parts):
-    B, S, H, D = 2, 96, 3, 64
+# Shapes: full and partial row runs of a block (a block takes 1024 / (D / 8)
+# rows, at most 128), head dims from one 16-byte unit per row to 256 units.
+@pytest.mark.parametrize("n_parts,shape,dtype", [
+    (1, (2, 96, 3, 64), torch.bfloat16), (2, (2, 96, 3, 64), torch.bfloat16), (3, (2, 96, 3, 64), torch.bfloat16),
+    (8, (2, 96, 3, 64), torch.bfloat16), (2, (1, 300, 2, 128), torch.float16), (3, (3, 17, 5, 8), torch.bfloat16),
+    (2, (1, 40, 2, 72), torch.float16), (2, (1, 9, 1, 2048), torch.bfloat16)])
+def test_merge_kernels_match_torch_merge(n_parts, shape, dtype):
+    B, S, H, D = shape
     g = torch.Generator().manual_seed(n_parts)
-    outs = [torch.randn(B, S, H, D, generator=g).to(torch.bfloat16).cuda() for _ in range(n_parts)]
+    outs = [torch.randn(B, S, H, D, generator=g).to(dtype).cuda() for _ in range(n_parts)]
     lses = [torch.randn(B, H, S, generator=g).cuda() * 3 for _ in range(n_parts)]
     lses[0][:, :, :5] = float("-inf")  # rows the first shard never saw
     if n_parts == 1:
         lses[0][0, 0, 7] = float("-inf")  # a row nobody saw
-    q = torch.empty(B, S, H, D, dtype=torch.bfloat16, device="cuda")
+    q = torch.empty(B, S, H, D, dtype=dtype, device="cuda")
     out, lse = parallel._merge_cuda(outs, lses, q, False, None, None)
     ref, lref = parallel.merge_partials([o.cpu() for o in outs], [l.cpu() for l in lses])
     torch.cuda.synchronize()
