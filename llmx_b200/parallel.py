@@ -101,18 +101,17 @@ def causal_key_range(seq_len: int, world: int, rank: int, align: int = 16) -> Tu
 
 
 def kv_split_ranges(seq_len: int, world: int, rank: int) -> List[Tuple[int, int]]:
-    """The key ranges of `rank` for a causal KV split over `world` ranks:
-    the zig-zag pair below four ranks, one contiguous range from four up.
+    """The key ranges of `rank` for a causal KV split over `world` ranks: one
+    contiguous, work-balanced range (``causal_key_range``), so each rank runs
+    one launch and holds one partial.
 
     Measured on B200 (B1 H32 S32768 D128 bf16, causal + ALiBi; slowest rank's
     kernel time as a fraction of a perfect split): 2 ranks 0.96 zig-zag /
-    0.92 contiguous, 4 ranks 0.82 / 0.82, 8 ranks 0.71 / 0.79.  With few
-    ranks the contiguous split's long last range (it holds every row's
-    diagonal block) runs a few percent slow; with many, the zig-zag deal's
-    second launch per rank costs more than that.
+    0.92 contiguous, 4 ranks 0.82 / 0.82, 8 ranks 0.71 / 0.79.  At 2 ranks
+    the zig-zag deal computes 4% faster, but one partial per rank lets the
+    merge gather 16-bit partials instead of all-reducing an fp32 buffer,
+    which saves more than that.
     """
-    if world < 4:
-        return zigzag_chunks(seq_len, world, rank)
     a, b = causal_key_range(seq_len, world, rank)
     return [(a, b)] if b > a else []
 
@@ -206,7 +205,9 @@ def kv_split_attention(
 def _merge_cuda(outs, lses, q, multi, group, out_dtype):
     """The merge on the GPU: row max of lse over every shard (all-reduce MAX),
     one scale kernel writing [num | wsum] for the local partials, one
-    all-reduce SUM of that buffer, one finish kernel."""
+    all-reduce SUM of that buffer, one finish kernel.  With one partial per
+    rank and at most three ranks the partials are all-gathered instead and
+    merged locally (no MAX / SUM all-reduce)."""
     import ctypes
 
     import torch.distributed as dist
@@ -216,6 +217,18 @@ def _merge_cuda(outs, lses, q, multi, group, out_dtype):
     B, S, H, D = q.shape
     if q.dtype not in (torch.float16, torch.bfloat16):
         raise RuntimeError("the KV-split merge takes fp16 or bf16 partials")
+    world = dist.get_world_size(group) if multi else 1
+    if multi and world <= 3 and len(outs) == 1:
+        # One partial per rank and few ranks: gathering every rank's 16-bit O
+        # and fp32 lse moves (world - 1) x (2 D + 4) bytes per row into each
+        # rank, against 2 (world - 1) / world x (4 D + 4) for the all-reduce
+        # of the fp32 [num | wsum] buffer; the merge then runs locally over
+        # all partials, in the same fp32 arithmetic.
+        o_all = torch.empty((world,) + tuple(q.shape), dtype=q.dtype, device=q.device)
+        l_all = torch.empty((world, B, H, S), dtype=torch.float32, device=q.device)
+        dist.all_gather_into_tensor(o_all, outs[0].contiguous(), group=group)
+        dist.all_gather_into_tensor(l_all, lses[0].contiguous(), group=group)
+        outs, lses, multi = list(o_all.unbind(0)), list(l_all.unbind(0)), False
     if lses:
         m = torch.stack(list(lses), 0).amax(0)
     else:

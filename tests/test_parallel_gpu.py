@@ -70,7 +70,7 @@ def test_kv_split_on_one_gpu_matches_unsplit():
     assert_close(out[0, rows], ref, torch.bfloat16, "kv split rows")
 
 
-def _nccl_rank(rank, world, port, S, H, D, path):
+def _nccl_rank(rank, world, port, S, H, D, path, split):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
 
@@ -81,7 +81,9 @@ def _nccl_rank(rank, world, port, S, H, D, path):
                             device_id=torch.device("cuda", rank))
     q, k, v = (rand(1, S, H, D, seed=s).cuda() for s in range(3))
     slopes = oracle.alibi_slopes(H).cuda()
-    chunks = parallel.zigzag_chunks(S, world, rank)
+    # zig-zag: two partials per rank, merged by all-reduce; ranges: one
+    # partial per rank, merged after an all-gather.
+    chunks = parallel.zigzag_chunks(S, world, rank) if split == "zigzag" else parallel.kv_split_ranges(S, world, rank)
     out, lse = parallel.kv_split_attention(q, [k[:, a:b] for a, b in chunks], [v[:, a:b] for a, b in chunks],
                                            [a for a, _ in chunks], S, D ** -0.5, alibi_slopes=slopes)
     torch.cuda.synchronize()
@@ -92,16 +94,21 @@ def _nccl_rank(rank, world, port, S, H, D, path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_kv_split_two_gpus_nccl(tmp_path):
+@pytest.mark.parametrize("split", ["zigzag", "ranges"])
+def test_kv_split_two_gpus_nccl(tmp_path, split):
     S, H, D = 8192, 4, 128
     path = str(tmp_path / "split.pt")
-    mp.spawn(_nccl_rank, args=(2, 29600 + os.getpid() % 1000, S, H, D, path), nprocs=2, join=True)
+    port = 29600 + os.getpid() % 1000 + (7 if split == "ranges" else 0)
+    mp.spawn(_nccl_rank, args=(2, port, S, H, D, path, split), nprocs=2, join=True)
     res = torch.load(path)
     q, k, v = (rand(1, S, H, D, seed=s).cuda() for s in range(3))
     full = torch.empty_like(q)
-    llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, alibi_slopes=oracle.alibi_slopes(H).cuda())
+    lse = torch.empty(1, H, S, device="cuda")
+    llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, alibi_slopes=oracle.alibi_slopes(H).cuda(),
+                                        lse=lse)
     torch.cuda.synchronize()
     assert (res["out"].float() - full.float().cpu()).abs().max().item() <= 2e-2
+    torch.testing.assert_close(res["lse"], lse.cpu(), atol=1e-3, rtol=0)
 
 
 # Shapes: full and partial row runs of a block (a block takes 1024 / (D / 8)
