@@ -426,7 +426,7 @@ def run_ours(args):
         "workloads": extras,
     }
     assert peak_unit
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=RESULT_OUT, flush=True)
 
 
 def run_reference(args):
@@ -467,10 +467,20 @@ def run_reference(args):
                                    f"the reference oracle's CPU path (ref_attention restated, fp32 torch)"},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=RESULT_OUT, flush=True)
+
+
+# The result line goes to the process's original standard output; everything
+# else written to file descriptor 1 (NCCL's version banner, library logs,
+# stray prints) is sent to standard error, so stdout carries the one JSON line.
+RESULT_OUT = sys.stdout
 
 
 def main():
+    global RESULT_OUT
+    sys.stdout.flush()
+    RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
