@@ -156,30 +156,27 @@ def measure_device(w, inp, steps, warmup, stream):
     return ms, out
 
 
-def measure_e2e(w, inp, steps, warmup, stream):
-    """Same call through the public API with host-resident inputs and output."""
+def measure_e2e(w, inp, steps, warmup, stream, chunks=4):
+    """Same workload through the public host-memory API
+    (llmx_b200.HostAttention: pinned host inputs and output, the batch cut
+    into `chunks` whose uploads, kernels and downloads overlap on three
+    streams).  Every step copies all of q, k, v up and all of o down."""
     import llmx_b200
 
     qh = inp.q.cpu().pin_memory()
     kh = inp.k.cpu().pin_memory()
     vh = inp.v.cpu().pin_memory()
     oh = torch.empty_like(qh).pin_memory()
-    qd, kd, vd = torch.empty_like(inp.q), torch.empty_like(inp.k), torch.empty_like(inp.v)
-    od = torch.empty_like(inp.q)
+    run = llmx_b200.HostAttention(qh, kh, inp.q.device, chunks=chunks)
     kw = dict(alibi_slopes=inp.alibi, causal=w.causal, q_lens=inp.q_lens, kv_lens=inp.kv_lens)
     times = []
-    with torch.cuda.stream(stream):
-        for i in range(warmup + steps):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            qd.copy_(qh, non_blocking=True)
-            kd.copy_(kh, non_blocking=True)
-            vd.copy_(vh, non_blocking=True)
-            llmx_b200.single_mha_attention_half(od, qd, kd, vd, w.sm_scale, **kw)
-            oh.copy_(od, non_blocking=True)
-            e1.record(stream)
-            if i >= warmup:
-                times.append((e0, e1))
+    for i in range(warmup + steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        run(oh, qh, kh, vh, w.sm_scale, stream=stream, **kw)
+        e1.record(stream)
+        if i >= warmup:
+            times.append((e0, e1))
     stream.synchronize()
     ms = [a.elapsed_time(b) for a, b in times]
     h2d = sum(t.numel() * t.element_size() for t in (qh, kh, vh))
@@ -281,47 +278,222 @@ def bench_workload(name, steps, warmup, rank, world, device, stream, peaks, with
 
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         n = len(ems)
+        e2e_ms = float(t.item()) / n
         res["e2e"] = {"value": work * world * n / (float(t.item()) * 1e-3) / scale, "unit": unit,
-                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                      "copy_gbs": (h2d + d2h) / (e2e_ms * 1e-3) / 1e9,
+                      "pipeline": "HostAttention: batch in 4 chunks, upload / kernel / download on 3 streams"}
     return res, w, inp
 
 
-def bench_kv_split(steps, warmup, rank, world, device, stream, peaks):
-    """Long-context prefill with its keys split over all ranks
-    (parallel.kv_split_ranges, NCCL log-sum-exp merge); strong scaling: the
-    job is one fixed sequence."""
-    import torch.distributed as dist
+def _max_over_ranks(values, world, device):
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
 
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def check_parity(out, lse, q, k, v, w, alibi, rows, heads, unsplit, world, device, cpu_blocks=2, seed=0):
+    """The checker of a multi-GPU leg, outside its timed region: this rank's
+    output rows `rows` of heads `heads` against (1) the single-GPU unsplit
+    kernel result `unsplit` on the same rows, (2) the fp32 oracle evaluated on
+    this GPU over every row and head this rank holds (oracle.attention_ref_chunked),
+    (3) the CPU oracle on `cpu_blocks` seeded 128-row blocks.  Tolerances: bf16
+    <= 2e-2 max-abs and <= 1e-2 mean-relative (the oracle), lse <= 2e-3.
+    Returns the parity block, worst case over ranks."""
+    import random
+
+    import oracle
+
+    r0, r1 = rows
+    hs = list(heads)
+    ref, lref = oracle.attention_ref_chunked(q, k, v, alibi=alibi, causal=w.causal, rows=(r0, r1), heads=hs)
+    err = (out.float() - ref).abs()
+    max_abs = float(err.max()) if err.numel() else 0.0
+    mean_rel = float(err.mean() / ref.abs().mean().clamp_min(1e-12)) if err.numel() else 0.0
+    fin = torch.isfinite(lref)
+    lse_err = float((lse[fin] - lref[fin]).abs().max()) if fin.any() else 0.0
+    vs_unsplit = float((out.float() - unsplit.float()).abs().max()) if out.numel() else 0.0
+    rng = random.Random(seed + r0)
+    cpu_err = 0.0
+    for _ in range(cpu_blocks if r1 > r0 else 0):
+        h = rng.choice(hs)
+        a = rng.randrange(r0, r1)
+        a = min(a, max(r0, r1 - 128))
+        e = min(r1, a + 128)
+        kv_end = e + (w.kv_len - w.q_len) if w.causal else w.kv_len
+        ro = oracle.attention_ref(q[0, a:e, h:h + 1].float().cpu(), k[0, :kv_end, h:h + 1].float().cpu(),
+                                  v[0, :kv_end, h:h + 1].float().cpu(), sm_scale=w.sm_scale,
+                                  alibi=None if alibi is None else alibi[h:h + 1].cpu(), causal=w.causal)
+        got = out[0, a - r0:e - r0, hs.index(h):hs.index(h) + 1].float().cpu()
+        cpu_err = max(cpu_err, float((got - ro).abs().max()))
+    worst = _max_over_ranks([max_abs, mean_rel, lse_err, vs_unsplit, cpu_err], world, device)
+    ok = worst[0] <= 2e-2 and worst[1] <= 1e-2 and worst[2] <= 2e-3 and worst[4] <= 2e-2
+    return {"max_abs": worst[0], "mean_rel": worst[1], "lse_max_abs": worst[2], "vs_unsplit_max_abs": worst[3],
+            "cpu_oracle_blocks_max_abs": worst[4], "cpu_oracle_blocks_per_rank": cpu_blocks, "ok": bool(ok),
+            "checked": "every row and head each rank holds vs the fp32 oracle on the GPU; the single-GPU kernel; "
+                       "seeded 128-row blocks vs the CPU oracle"}
+
+
+def _timed(fn, steps, warmup, stream, world, sync=None):
+    """Per-step CUDA-event time of fn() on `stream` (a barrier before each
+    step when world > 1); returns (ms per step, max over ranks; per-step
+    phase marks from the last step)."""
+    times = []
+    with torch.cuda.stream(stream):
+        for i in range(warmup + steps):
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            marks = fn()
+            e1.record(stream)
+            if i >= warmup:
+                times.append((e0, e1, marks))
+    stream.synchronize()
+    total = sum(a.elapsed_time(b) for a, b, _ in times)
+    phases = {}
+    for e0, _, marks in times:
+        prev = e0
+        for name, ev in marks or []:
+            phases[name] = phases.get(name, 0.0) + prev.elapsed_time(ev) / len(times)
+            prev = ev
+    names = sorted(phases)
+    vals = _max_over_ranks([total / steps] + [phases[n] for n in names], world, stream.device)
+    return vals[0], dict(zip(names, vals[1:]))
+
+
+def bench_kv_split(steps, warmup, rank, world, device, stream, peaks, unsplit):
+    """Long-context prefill (B1 H32 S32768 D128 bf16, causal + ALiBi) with its
+    keys split over all ranks (parallel.KVSplitPlan.contiguous: one
+    work-balanced key range per rank, each rank computing only the rows that
+    can see its keys, row slices exchanged point to point over NCCL, merged
+    by the library's log-sum-exp kernel); strong scaling.  Timed with the
+    output row-sharded (the headline of the leg) and replicated (plus an
+    NCCL all-gather of the slices)."""
     from llmx_b200 import parallel
     from llmx_b200.workloads import WORKLOADS, flops, make_inputs
 
     w = WORKLOADS["long_prefill_bf16_b1_h32_s32768_d128"]
     inp = make_inputs(w, device)
     S = w.q_len
-    chunks = parallel.kv_split_ranges(S, world, rank)
-    kc = [inp.k[:, a:b] for a, b in chunks]
-    vc = [inp.v[:, a:b] for a, b in chunks]
-    offs = [a for a, _ in chunks]
+    plan = parallel.KVSplitPlan.contiguous(S, world)
+    mine = plan.chunks[rank]
+    kc = [inp.k[:, a:b] for a, b in mine]
+    vc = [inp.v[:, a:b] for a, b in mine]
+    fl = flops(w, [S], [S])
+    res = {"kernel": "tcgen05 (row-restricted partial) + NCCL point-to-point row slices + lse merge kernel",
+           "plan": {"key_ranges": [list(c) for c in plan.chunks], "first_rows": [plan.first_row(r) for r in range(world)],
+                    "slice_rows": plan.slice_rows}}
+    for output in ("sharded", "replicated"):
+        holder = {}
+
+        def step():
+            marks = []
+            holder["r"] = parallel.kv_split_attention(inp.q, kc, vc, plan, w.sm_scale, alibi_slopes=inp.alibi,
+                                                      output=output, timings=marks)
+            return marks
+
+        per, phases = _timed(step, steps, warmup, stream, world)
+        res[output] = {"value": fl / (per * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": per,
+                       "phase_ms_max_over_ranks": phases}
+        if output == "sharded":
+            out, lse, (lo, hi) = holder["r"]
+            res["parity"] = check_parity(out, lse, inp.q, inp.k, inp.v, w, inp.alibi, (lo, hi), range(w.n_heads),
+                                         unsplit[:, lo:hi], world, device)
+        del holder
+    sh = res["sharded"]
+    res.update({"value": sh["value"], "unit": "TFLOP/s", "ms_per_step": sh["ms_per_step"], "scaling": "strong",
+                "output": "row-sharded (each rank holds the merged rows of its slice); 'replicated' adds the all-gather",
+                "roofline": {"bound": "tensor", "achieved": fl / world / (sh["ms_per_step"] * 1e-3) / 1e12,
+                             "peak": peaks["bf16_tflops"], "unit": "TFLOP/s per GPU",
+                             "frac": fl / world / (sh["ms_per_step"] * 1e-3) / 1e12 / peaks["bf16_tflops"]}})
+    return res
+
+
+def bench_head_split(steps, warmup, rank, world, device, stream, peaks, unsplit):
+    """Long-context prefill with its 32 heads dealt over the ranks
+    (parallel.head_range: 4 heads per GPU at 8 GPUs), no collective; strong
+    scaling of one fixed sequence."""
+    import llmx_b200
+    from llmx_b200 import parallel
+    from llmx_b200.workloads import WORKLOADS, flops, make_inputs
+
+    w = WORKLOADS["long_prefill_bf16_b1_h32_s32768_d128"]
+    inp = make_inputs(w, device)
+    S = w.q_len
+    h0, h1 = parallel.head_range(w.n_heads, world, rank)
+    out = torch.empty_like(inp.q[:, :, h0:h1])
+
+    def step():
+        llmx_b200.single_mha_attention_half(out, inp.q[:, :, h0:h1], inp.k[:, :, h0:h1], inp.v[:, :, h0:h1],
+                                            w.sm_scale, alibi_slopes=inp.alibi[h0:h1])
+        return None
+
+    per, _ = _timed(step, steps, warmup, stream, world)
+    fl = flops(w, [S], [S])
+    lse = torch.empty(1, h1 - h0, S, device=device)
+    llmx_b200.single_mha_attention_half(out, inp.q[:, :, h0:h1], inp.k[:, :, h0:h1], inp.v[:, :, h0:h1],
+                                        w.sm_scale, alibi_slopes=inp.alibi[h0:h1], lse=lse)
+    parity = check_parity(out, lse, inp.q, inp.k, inp.v, w, inp.alibi, (0, S), range(h0, h1), unsplit[:, :, h0:h1],
+                          world, device)
+    return {"kernel": "tcgen05, heads [h0, h1) per rank, no collective", "heads_per_rank": h1 - h0,
+            "value": fl / (per * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": per, "scaling": "strong",
+            "roofline": {"bound": "tensor", "achieved": fl / world / (per * 1e-3) / 1e12,
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s per GPU",
+                         "frac": fl / world / (per * 1e-3) / 1e12 / peaks["bf16_tflops"]},
+            "parity": parity}
+
+
+def bench_strong_units(steps, warmup, rank, world, device, stream, peaks):
+    """The Llama-7B-shaped prefill as ONE fixed job (B8 H32 S2048, the same
+    seed on every rank) whose 256 (batch, head) units are dealt over the ranks
+    (parallel.shard_units / run_units), no collective; strong scaling.
+    L2 flushed between steps."""
+    import llmx_b200
+    from llmx_b200 import parallel
+    from llmx_b200.workloads import WORKLOADS, flops, make_inputs
+
+    w = WORKLOADS[HEADLINE]
+    inp = make_inputs(w, device)  # same seed on every rank: one job
+    start, end = parallel.shard_units(w.batch, w.n_heads, world, rank)
+    out = torch.zeros_like(inp.q)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    n_launch = [0]
     times = []
     with torch.cuda.stream(stream):
         for i in range(warmup + steps):
-            dist.barrier()
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.barrier()
+            flush.fill_(i & 0xFF)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            parallel.kv_split_attention(inp.q, kc, vc, offs, S, w.sm_scale, alibi_slopes=inp.alibi)
+            n_launch[0] = parallel.run_units(out, inp.q, inp.k, inp.v, start, end, w.sm_scale, causal=w.causal)
             e1.record(stream)
             if i >= warmup:
                 times.append((e0, e1))
     stream.synchronize()
-    ms = torch.tensor([sum(a.elapsed_time(b) for a, b in times)], dtype=torch.float64, device=device)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    per = float(ms.item()) / steps
-    fl = flops(w, [S], [S])
-    return {"kernel": "tcgen05 + NCCL lse merge", "value": fl / (per * 1e-3) / 1e12, "unit": "TFLOP/s",
-            "ms_per_step": per, "scaling": "strong", "chunks_per_rank": len(chunks),
+    per = _max_over_ranks([sum(a.elapsed_time(b) for a, b in times) / steps], world, device)[0]
+    fl = flops(w, inp.q_lens_list, inp.kv_lens_list)
+    full = torch.empty_like(inp.q)
+    llmx_b200.single_mha_attention_half(full, inp.q, inp.k, inp.v, w.sm_scale, causal=w.causal)
+    torch.cuda.synchronize(device)
+    same = all(torch.equal(out[b0:b1, :, h0:h1], full[b0:b1, :, h0:h1])
+               for b0, b1, h0, h1 in parallel.unit_runs(start, end, w.n_heads))
+    same = _max_over_ranks([0.0 if same else 1.0], world, device)[0] == 0.0
+    return {"kernel": "tcgen05 on this rank's (batch, head) units", "units_per_rank": end - start,
+            "launches_per_step": n_launch[0], "value": fl / (per * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": per, "scaling": "strong",
             "roofline": {"bound": "tensor", "achieved": fl / world / (per * 1e-3) / 1e12,
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s per GPU",
-                         "frac": fl / world / (per * 1e-3) / 1e12 / peaks["bf16_tflops"]}}
+                         "frac": fl / world / (per * 1e-3) / 1e12 / peaks["bf16_tflops"]},
+            "parity": {"bitwise_equal_to_single_gpu_call": same, "ok": same}}
 
 
 def bench_convert(steps, warmup, rank, world, device, stream, peaks):
@@ -358,6 +530,16 @@ def bench_convert(steps, warmup, rank, world, device, stream, peaks):
                          "frac": achieved / peaks["hbm_gbs"], "traffic": None, "algorithmic": nbytes}}
 
 
+def headline_config(w, world):
+    """The `config` of the headline line, shared by both arms."""
+    return {"workload": w.name, "batch_per_gpu": w.batch, "heads": w.n_heads, "kv_heads": w.n_kv_heads,
+            "seq_len": w.q_len, "head_dim": w.head_dim, "causal": w.causal, "alibi": w.alibi,
+            "parallelism": f"replica per GPU: each of {world} GPU(s) runs the whole workload on its own seed, "
+                           "no collective (weak scaling); the fixed job split over the GPUs is under "
+                           f"workloads.llama7b_prefill_strong_{world}gpu",
+            "l2": "flushed between steps (256 MiB write)"}
+
+
 def run_ours(args):
     rank, world, local = dist_info()
     device = torch.device("cuda", local)
@@ -373,8 +555,11 @@ def run_ours(args):
     peaks, peak_src = load_peaks()
     stream = torch.cuda.Stream(device)
     headline = args.workload or HEADLINE
+    if args.profile_only:
+        args.no_extra = True
     with ClockSampler(local) as clocks:
-        head, w, inp = bench_workload(headline, args.steps, args.warmup, rank, world, device, stream, peaks, True)
+        head, w, inp = bench_workload(headline, args.steps, args.warmup, rank, world, device, stream, peaks,
+                                      not args.profile_only)
     extras = {}
     if not args.no_extra:
         for name in EXTRA:
@@ -387,11 +572,26 @@ def run_ours(args):
     if not args.no_extra:
         extras["dtype_convert_fp32_to_bf16_256Mi"] = bench_convert(args.steps, args.warmup, rank, world, device,
                                                                    stream, peaks)
+    if not args.no_extra:
+        extras[f"llama7b_prefill_strong_{world}gpu"] = bench_strong_units(args.steps, args.warmup, rank, world,
+                                                                         device, stream, peaks)
     if world > 1 and not args.no_extra:
-        extras["long_prefill_kv_split_" + str(world) + "gpu"] = bench_kv_split(
-            3, min(args.warmup, 3), rank, world, device, stream, peaks)
+        # the single-GPU result every rank checks its share of the long sequence against
+        from llmx_b200.workloads import WORKLOADS as _W, make_inputs as _mk
+
+        lw = _W["long_prefill_bf16_b1_h32_s32768_d128"]
+        li = _mk(lw, device)
+        unsplit = torch.empty_like(li.q)
+        llmx_b200.single_mha_attention_half(unsplit, li.q, li.k, li.v, lw.sm_scale, alibi_slopes=li.alibi)
+        torch.cuda.synchronize(device)
+        del li
+        extras[f"long_prefill_kv_split_{world}gpu"] = bench_kv_split(3, min(args.warmup, 3), rank, world, device,
+                                                                     stream, peaks, unsplit)
+        extras[f"long_prefill_head_split_{world}gpu"] = bench_head_split(3, min(args.warmup, 3), rank, world,
+                                                                         device, stream, peaks, unsplit)
+        del unsplit
     cpu = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.profile_only:
         sample = cpu_units_sample(w, inp, args.cpu_units)
         rate, secs, threads = cpu_oracle_rate(w, sample, repeats=args.cpu_repeats)
         cpu = {"value": rate / (1e9 if w.is_decode else 1e12), "unit": head["unit"], "cores": threads,
@@ -413,13 +613,10 @@ def run_ours(args):
         "scaling": "weak", "vs_baseline": None,
         "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[w.dtype],
         "data": "synthetic: seeded N(0,1) inputs of the workload's shape (rank-specific seed per GPU)",
-        "config": {"workload": w.name, "batch_per_gpu": w.batch, "heads": w.n_heads, "kv_heads": w.n_kv_heads,
-                   "seq_len": w.q_len, "head_dim": w.head_dim, "causal": w.causal, "alibi": w.alibi,
-                   "parallelism": f"batch x head shards over {world} GPU(s), no data-path collective",
-                   "l2": "flushed between steps (256 MiB write)"},
+        "config": headline_config(w, world),
         "kernel": head["kernel"],
         "roofline": head["roofline"],
-        "e2e": head["e2e"],
+        "e2e": head.get("e2e"),
         "gpu_launches": head["launches_per_step"] * args.steps,
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
@@ -460,8 +657,7 @@ def run_reference(args):
         "ms_per_step": tot_secs / len(rates) * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic: seeded N(0,1) inputs of the workload's shape",
-        "config": {"workload": w.name, "batch_per_gpu": w.batch, "heads": w.n_heads, "seq_len": w.q_len,
-                   "head_dim": w.head_dim, "causal": w.causal, "alibi": w.alibi},
+        "config": headline_config(w, world),
         "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
                          "sample": f"each step: {len(sample)} seeded (batch, head) units of {w.name} through "
                                    f"the reference oracle's CPU path (ref_attention restated, fp32 torch)"},
@@ -488,6 +684,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default=None)
     ap.add_argument("--no-extra", action="store_true", help="skip the secondary workloads")
+    ap.add_argument("--profile-only", action="store_true",
+                    help="device-timed steps of the one workload only (no e2e, cpu_baseline or extras): for ncu")
     ap.add_argument("--cpu-units", type=int, default=64, help="units in the cpu_baseline sample")
     ap.add_argument("--cpu-repeats", type=int, default=6, help="passes over the cpu_baseline sample")
     ap.add_argument("--ref-units", type=int, default=32, help="units per step of the reference arm")

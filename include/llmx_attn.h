@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define LLMX_ATTN_ABI_VERSION 2
+#define LLMX_ATTN_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define LLMX_API __attribute__((visibility("default")))
@@ -53,7 +53,7 @@ typedef enum llmx_attn_algo {
   LLMX_ALGO_AUTO = 0,
   LLMX_ALGO_SIMT = 1,    /* fp32-accumulating CUDA-core kernel, every shape  */
   LLMX_ALGO_DECODE = 2,  /* split-KV decode, max_q_len == 1, fp16/bf16       */
-  LLMX_ALGO_TCGEN05 = 3  /* TMA + tcgen05/TMEM prefill, fp16/bf16, D 64/128 */
+  LLMX_ALGO_TCGEN05 = 3  /* TMA + tcgen05/TMEM prefill, fp16/bf16, D 64/128/256 */
 } llmx_attn_algo;
 
 /*
@@ -144,11 +144,18 @@ LLMX_API llmx_status llmx_single_mha_attention_c(void *output, const void *q, co
  * in one static device array of LLMX_DECODE_NOALLOC_SCRATCH_BYTES per GPU,
  * held by every GPU that loads the library until the process exits.
  *  - Requests needing more scratch than that are refused with
- *    LLMX_ERR_WORKSPACE_TOO_SMALL (need = n_splits * batch * n_heads *
- *    (head_dim + 1) * 4 bytes; 256-key splits).
+ *    LLMX_ERR_WORKSPACE_TOO_SMALL.  The need is n_splits * batch * n_heads *
+ *    (head_dim + 1) * 4 bytes, where a split holds between 64 and 256 keys:
+ *    256, halved (down to 64) while batch x kv-head units alone cannot give
+ *    the GPU four waves of work, so small batches need up to four times the
+ *    256-key figure.  llmx_attn_workspace_size returns the exact need for a
+ *    request (the same plan); compare it with the constant below.
  *  - The first call on a device looks up the array's device address
- *    (cudaGetSymbolAddress, once per device, with that device current); make
- *    that first call before any stream capture.
+ *    (cudaGetSymbolAddress, with that device current) and keeps it once the
+ *    lookup succeeds; a failed lookup is retried on the next call.  Make
+ *    that first call before any stream capture.  After cudaDeviceReset the
+ *    kept address is stale: do not call this entry point again in that
+ *    process.
  *  - All calls on a device share the array: calls that overlap on the GPU
  *    (different streams, or concurrent host threads) race and corrupt each
  *    other's results.  p->workspace is ignored.
@@ -156,25 +163,35 @@ LLMX_API llmx_status llmx_single_mha_attention_c(void *output, const void *q, co
 #define LLMX_DECODE_NOALLOC_SCRATCH_BYTES (32u << 20)
 LLMX_API llmx_status llmx_attn_decode_noalloc(const llmx_attn_params *p, void *stream);
 
-/* Log-sum-exp merge of attention partials over disjoint key sets (keys
- * split across calls or GPUs), in two steps around a cross-GPU SUM of
- * [num | wsum].  No counterpart in the reference (it has no key splitting);
- * the algebra is its online-softmax rescale (softmax.h:53-110) applied
- * across shards.
- *   outs[c]  : [batch, seq, n_heads, head_dim] partial O (fp16/bf16, contiguous)
- *   lses[c]  : [batch, n_heads, seq] fp32 natural-log lse (-inf: no key seen)
- *   row_max  : [batch, n_heads, seq] fp32 max of lse over every shard
- *   num      : [batch, seq, n_heads, head_dim] fp32 = sum_c exp(lse_c - m) O_c
- *   wsum     : [batch, n_heads, seq] fp32 = sum_c exp(lse_c - m)
- * merge_finish writes out = num / wsum (0 where wsum == 0) in the partials'
- * dtype and, if lse_out is not NULL, lse = m + log(wsum).  n_parts <= 8. */
-LLMX_API llmx_status llmx_attn_lse_merge_scale(int32_t n_parts, const void *const *outs, const float *const *lses,
-                                               const float *row_max, int32_t dtype, int32_t batch, int32_t seq,
-                                               int32_t n_heads, int32_t head_dim, float *num, float *wsum,
-                                               void *stream);
-LLMX_API llmx_status llmx_attn_lse_merge_finish(const float *num, const float *wsum, const float *row_max,
-                                                int32_t dtype, int32_t batch, int32_t seq, int32_t n_heads,
-                                                int32_t head_dim, void *out, float *lse_out, void *stream);
+/* Log-sum-exp merge of attention partials over disjoint key sets (a
+ * sequence's keys split across calls or GPUs).  No counterpart in the
+ * reference (it has no key splitting); the algebra is its online-softmax
+ * rescale (softmax.h:53-110) applied across shards:
+ *   m = max_c lse_c,  w_c = exp(lse_c - m),  O = sum_c w_c O_c / sum_c w_c,
+ *   lse = m + log(sum_c w_c).
+ * Part c covers output rows [row_lo, row_hi) of every (batch, head); for
+ * output row s in that range its O element (b, s, h, d) is at
+ *   o[b*o_stride[0] + (s - row_lo)*o_stride[1] + h*o_stride[2] + d]
+ * and its natural-log lse (-inf: the part saw no key) at
+ *   lse[b*lse_stride[0] + h*lse_stride[1] + (s - row_lo)].
+ * Rows outside a part's range get no term from it, and a part's O is not
+ * read where its lse is -inf, so those rows may hold anything.  Output:
+ * out [batch, seq, n_heads, head_dim] with element strides out_stride
+ * (batch, seq, head; multiples of 8), in the partials' dtype (fp16/bf16),
+ * 0 where no part saw a key; lse_out (NULL or contiguous fp32
+ * [batch, n_heads, seq]) = -inf there.  n_parts <= 16; head_dim a
+ * multiple of 8; O pointers and strides 16-byte aligned. */
+typedef struct llmx_merge_part {
+  const void *o;
+  const float *lse;
+  int64_t o_stride[3];   /* elements: batch, row, head */
+  int64_t lse_stride[2]; /* elements: batch, head      */
+  int32_t row_lo, row_hi;
+} llmx_merge_part;
+
+LLMX_API llmx_status llmx_attn_lse_merge(int32_t n_parts, const llmx_merge_part *parts, int32_t dtype,
+                                         int32_t batch, int32_t seq, int32_t n_heads, int32_t head_dim, void *out,
+                                         const int64_t *out_stride, float *lse_out, void *stream);
 
 /* Element-type conversion of n contiguous elements between fp32, fp16 and
  * bf16 (round to nearest even), enqueued on `stream`.  Replaces the

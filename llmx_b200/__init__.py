@@ -7,6 +7,7 @@ path.  Build it with `python -m llmx_b200.build`.
 """
 from ._lib import LlmxError, load  # noqa: F401
 from .ops import attention, convert, device_status, selected_algo, single_mha_attention_half  # noqa: F401
+from .streaming import HostAttention, attention_from_host  # noqa: F401
 
 __all__ = ["single_mha_attention_half", "attention", "convert", "selected_algo", "device_status", "LlmxError",
-           "load"]
+           "load", "HostAttention", "attention_from_host"]

@@ -65,6 +65,19 @@ class AttnParams(ctypes.Structure):
     ]
 
 
+class MergePart(ctypes.Structure):
+    """Mirror of ``llmx_merge_part``."""
+
+    _fields_ = [
+        ("o", _vp),
+        ("lse", _vp),
+        ("o_stride", _i64x3),
+        ("lse_stride", ctypes.c_int64 * 2),
+        ("row_lo", _i32),
+        ("row_hi", _i32),
+    ]
+
+
 # Every function include/llmx_attn.h declares: name -> (restype, argtypes).
 SIGNATURES = {
     "llmx_attn_params_init": (_i32, [ctypes.POINTER(AttnParams)]),
@@ -77,11 +90,11 @@ SIGNATURES = {
     ),
     "llmx_attn_select_algo": (_i32, [ctypes.POINTER(AttnParams), ctypes.POINTER(_i32)]),
     "llmx_attn_decode_noalloc": (_i32, [ctypes.POINTER(AttnParams), _vp]),
-    "llmx_attn_lse_merge_scale": (
+    "llmx_attn_lse_merge": (
         _i32,
-        [_i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp],
+        [_i32, ctypes.POINTER(MergePart), _i32, _i32, _i32, _i32, _i32, _vp, ctypes.POINTER(ctypes.c_int64), _vp,
+         _vp],
     ),
-    "llmx_attn_lse_merge_finish": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
     "llmx_convert": (_i32, [_vp, _i32, _vp, _i32, ctypes.c_size_t, _vp]),
     "llmx_attn_device_status": (_i32, [_i32, _i32]),
     "llmx_status_string": (ctypes.c_char_p, [_i32]),

@@ -170,7 +170,7 @@ llmx_status choose(const AttnArgs &a, int requested, int *algo) {
                 "aligned rows");
   if (requested == LLMX_ALGO_TCGEN05 && !sm100_supports(a))
     return fail(LLMX_ERR_UNSUPPORTED,
-                "tcgen05 kernel needs fp16/bf16, head_dim 64 or 128 and 16-byte aligned rows");
+                "tcgen05 kernel needs fp16/bf16, head_dim 64, 128 or 256, sm_scale > 0 and 16-byte aligned rows");
   *algo = requested;
   return LLMX_OK;
 }

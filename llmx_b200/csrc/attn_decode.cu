@@ -364,20 +364,27 @@ static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / 
 
 constexpr int kMaxNoAllocDevices = 64;
 float *g_noalloc_ptr[kMaxNoAllocDevices];
-cudaError_t g_noalloc_status[kMaxNoAllocDevices];
-std::once_flag g_noalloc_once[kMaxNoAllocDevices];
+std::mutex g_noalloc_mu;
 
 // Device address of the scratch array on `dev` (which must be current).
-// Looked up once per device; cudaGetSymbolAddress allocates nothing.
+// Only a successful lookup is kept; a failed one (for example a first call
+// made during stream capture) is retried by the next call.
+// cudaGetSymbolAddress allocates nothing.
 cudaError_t noalloc_scratch(int dev, float **out) {
-  std::call_once(g_noalloc_once[dev], [dev] {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
     void *p = nullptr;
-    g_noalloc_status[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    g_noalloc_ptr[dev] = g_noalloc_status[dev] == cudaSuccess ? static_cast<float *>(p) : nullptr;
-  });
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      cudaGetLastError();  // the failed lookup must not poison the next launch check
+      *out = nullptr;
+      return e;
+    }
+    if (p == nullptr) return cudaErrorInvalidSymbol;
+    g_noalloc_ptr[dev] = static_cast<float *>(p);
+  }
   *out = g_noalloc_ptr[dev];
-  if (g_noalloc_status[dev] == cudaSuccess && *out == nullptr) return cudaErrorInvalidSymbol;
-  return g_noalloc_status[dev];
+  return cudaSuccess;
 }
 
 }  // namespace

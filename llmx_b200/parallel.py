@@ -1,25 +1,32 @@
 """Multi-GPU partitioning of the attention forward (one process per GPU).
 
-Two ways the work splits across GPUs of one node:
+Three ways the work splits across the GPUs of one node:
 
 * **batch x head shards** (independent units, no communication): every
   (batch, head) pair is an independent attention problem.  ``shard_units``
-  gives each rank a contiguous, balanced slice of the flattened units; each
-  rank runs the kernel on its slice.
-* **KV split** for long sequences: each rank holds the full query block and a
-  share of the keys, computes (O_r, lse_r) over its keys with the kernel
-  (``kv_offset`` / ``kv_total`` place the shard's keys at their global
-  positions for the causal diagonal and ALiBi), and the partials are merged
+  gives each rank a contiguous, balanced slice of the flattened units and
+  ``run_units`` runs the kernel on such a slice (one launch per batch run).
+* **head split** of one long sequence (``head_range``): each rank takes a
+  contiguous block of heads, whole GQA groups, and runs the kernel on it; no
+  communication.
+* **KV split** of one long sequence (``KVSplitPlan`` + ``kv_split_attention``):
+  rank r holds a share of the keys.  Under the causal mask a query row below
+  the rank's first key sees none of them, so the rank computes its partial
+  (O_r, lse_r) only for the rows from ``plan.first_row(r)`` on.  The output
+  rows are dealt in equal slices, one per rank; each rank sends every other
+  rank the rows of its partial that fall in that rank's slice (NCCL
+  point-to-point in one group), and merges the partials of its own slice
   exactly with the log-sum-exp rule
 
-      lse = log sum_r exp(lse_r),   O = sum_r exp(lse_r - lse) O_r
+      m = max_r lse_r,  O = sum_r exp(lse_r - m) O_r / sum_r exp(lse_r - m)
 
-  as NCCL all-reduce MAX of lse_r, a local rescale, and one all-reduce SUM of
-  [O_r * w_r | w_r] (w_r = exp(lse_r - max)).  For causal masking each rank
-  takes one contiguous key range sized for equal visible work
-  (``causal_key_range``: early keys are seen by more queries, so the first
-  ranges are shorter); ``zigzag_chunks`` gives the classic two-chunk deal
-  (with 2n chunks, rank g takes chunks g and 2n-1-g) for callers that want it.
+  in one kernel.  The result is row-sharded (``output="sharded"``) or, after
+  an all-gather of the slices, on every rank (``output="replicated"``).
+
+Every collective or point-to-point step is derived from the plan, which
+every rank computes identically, so all ranks issue matching NCCL calls
+whatever their local key count (a rank without keys sends nothing and still
+receives its slice).
 
 The reference has no multi-GPU code; its kernel already streams keys through
 an online softmax inside one SM (single_mha_kernel.cuh:294-340), and the
@@ -29,12 +36,16 @@ shards instead of across blocks (softmax.h:53-110).
 
 from __future__ import annotations
 
+import ctypes
 import math
+from dataclasses import dataclass
 from typing import List, Optional, Sequence, Tuple
 
 import torch
 
-from . import ops
+from . import _lib, ops
+
+# ---------------------------------------------------------------- unit shards
 
 
 def shard_units(batch: int, heads: int, world: int, rank: int) -> Tuple[int, int]:
@@ -50,6 +61,54 @@ def shard_units(batch: int, heads: int, world: int, rank: int) -> Tuple[int, int
     start = rank * base + min(rank, extra)
     end = start + base + (1 if rank < extra else 0)
     return start, end
+
+
+def unit_runs(start: int, end: int, heads: int) -> List[Tuple[int, int, int, int]]:
+    """The unit range [start, end) as launches: (b0, b1, h0, h1) boxes of whole
+    head runs, at most three (a partial first batch, whole batches, a partial
+    last batch)."""
+    runs = []
+    u = start
+    while u < end:
+        b, h = divmod(u, heads)
+        if h == 0 and end - u >= heads:
+            nb = (end - u) // heads
+            runs.append((b, b + nb, 0, heads))
+            u += nb * heads
+        else:
+            h1 = min(heads, h + (end - u))
+            runs.append((b, b + 1, h, h1))
+            u += h1 - h
+    return runs
+
+
+def run_units(out, q, k, v, start: int, end: int, sm_scale: float, *, alibi_slopes=None, **kw) -> int:
+    """Attention of the (batch, head) units [start, end) of [B, S, H, D] tensors,
+    written into the same units of `out`; other units are untouched.  Returns
+    the number of launches.  With GQA every head run must cover whole groups."""
+    H, Hkv = q.shape[2], k.shape[2]
+    g = H // Hkv
+    n = 0
+    for b0, b1, h0, h1 in unit_runs(start, end, H):
+        if h0 % g or h1 % g:
+            raise ValueError("a unit shard must hold whole GQA groups")
+        a = None if alibi_slopes is None else alibi_slopes[h0:h1]
+        ops.single_mha_attention_half(out[b0:b1, :, h0:h1], q[b0:b1, :, h0:h1], k[b0:b1, :, h0 // g:h1 // g],
+                                      v[b0:b1, :, h0 // g:h1 // g], sm_scale, alibi_slopes=a, **kw)
+        n += 1
+    return n
+
+
+def head_range(n_heads: int, world: int, rank: int, group: int = 1) -> Tuple[int, int]:
+    """Contiguous heads [h0, h1) of `rank` when whole GQA groups of `group`
+    heads are dealt over `world` ranks (sizes differ by at most one group)."""
+    if n_heads % group:
+        raise ValueError("group must divide n_heads")
+    g0, g1 = shard_units(1, n_heads // group, world, rank)
+    return g0 * group, g1 * group
+
+
+# ---------------------------------------------------------------- key shards
 
 
 def zigzag_chunks(seq_len: int, world: int, rank: int, align: int = 128) -> List[Tuple[int, int]]:
@@ -78,184 +137,296 @@ def causal_key_range(seq_len: int, world: int, rank: int, align: int = 16) -> Tu
     `seq_len` queries attend over `seq_len` keys (key j is seen by the
     seq_len - j queries at or below it).
 
-    Every rank holds all queries, so unlike the zig-zag deal one range per
-    rank suffices: one kernel launch and one partial per rank.  Range
-    boundaries are rounded to multiples of `align`; the ranges cover every
-    key exactly once (empty ranges are possible for tiny sequences).
+    Range boundaries are multiples of `align`, and when seq_len >= world *
+    align every rank gets at least one align block (the balanced boundaries
+    are clamped into [r * align, seq_len - (world - r) * align]).  Shorter
+    sequences are too short to split that finely: the ranges then come from
+    the same rule over the ranks that get a block each, the last ones empty.
+    The ranges cover every key exactly once.
     """
     if world < 1 or not 0 <= rank < world:
         raise ValueError("rank must be in [0, world)")
+    blocks = -(-seq_len // align)
+    eff = max(1, min(world, blocks))  # ranks that can get at least one block
+    if rank >= eff:
+        return seq_len, seq_len
     total = seq_len * (seq_len + 1) / 2
     b = 2 * seq_len + 1
 
     def bound(r: int) -> int:
         if r <= 0:
             return 0
-        if r >= world:
+        if r >= eff:
             return seq_len
-        # smallest x with x * seq_len - x * (x - 1) / 2 >= r * total / world
-        x = (b - math.sqrt(max(0.0, b * b - 8 * r * total / world))) / 2
-        return min(seq_len, int(round(x / align)) * align)
+        # smallest x with x * seq_len - x * (x - 1) / 2 >= r * total / eff
+        x = (b - math.sqrt(max(0.0, b * b - 8 * r * total / eff))) / 2
+        x = int(round(x / align)) * align
+        return max(r * align, min(x, seq_len - (eff - r) * align, seq_len))
 
     return bound(rank), bound(rank + 1)
 
 
 def kv_split_ranges(seq_len: int, world: int, rank: int) -> List[Tuple[int, int]]:
     """The key ranges of `rank` for a causal KV split over `world` ranks: one
-    contiguous, work-balanced range (``causal_key_range``), so each rank runs
-    one launch and holds one partial.
-
-    Measured on B200 (B1 H32 S32768 D128 bf16, causal + ALiBi; slowest rank's
-    kernel time as a fraction of a perfect split): 2 ranks 0.96 zig-zag /
-    0.92 contiguous, 4 ranks 0.82 / 0.82, 8 ranks 0.71 / 0.79.  At 2 ranks
-    the zig-zag deal computes 4% faster, but one partial per rank lets the
-    merge gather 16-bit partials instead of all-reducing an fp32 buffer,
-    which saves more than that.
-    """
+    contiguous, work-balanced range (``causal_key_range``), or none for a
+    rank left without keys by a sequence shorter than world * 16 keys."""
     a, b = causal_key_range(seq_len, world, rank)
     return [(a, b)] if b > a else []
 
 
-def merge_partials(outs: Sequence[torch.Tensor], lses: Sequence[torch.Tensor]):
-    """Exact merge of attention partials over disjoint key sets (one rank).
+@dataclass(frozen=True)
+class KVSplitPlan:
+    """Who holds which keys and who owns which output rows, for one sequence
+    of `q_len` queries over `kv_len` keys split over `world` ranks.
 
-    outs: [B, S, H, D] each (any float type); lses: [B, H, S] fp32 natural-log
-    (-inf where a row saw no key).  Returns (O fp32 [B, S, H, D], lse [B, H, S]).
-    """
-    lse = torch.stack(list(lses), 0)  # [n, B, H, S]
-    m = lse.amax(0)
-    m_safe = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
-    w = torch.exp(lse - m_safe)  # exp(-inf) = 0 for empty partials
-    wsum = w.sum(0)
-    num = None
-    for o, wi in zip(outs, w):
-        term = o.float() * wi.permute(0, 2, 1).unsqueeze(-1)
-        num = term if num is None else num + term
-    inv = torch.where(wsum > 0, 1.0 / wsum, torch.zeros_like(wsum))
-    out = num * inv.permute(0, 2, 1).unsqueeze(-1)
-    lse_out = torch.where(wsum > 0, m_safe + torch.log(wsum), torch.full_like(m, float("-inf")))
-    return out, lse_out
+    chunks[r]: the key ranges [a, b) rank r holds (ascending).  Output rows
+    are dealt in slices of `slice_rows` (the last one shorter or empty).
+    Under the causal mask (bottom-right: row i sees key j <= i + kv_len -
+    q_len) a rank computes its partial only for rows >= first_row(r)."""
+
+    q_len: int
+    kv_len: int
+    world: int
+    chunks: Tuple[Tuple[Tuple[int, int], ...], ...]
+    causal: bool = True
+
+    @classmethod
+    def contiguous(cls, seq_len: int, world: int, causal: bool = True) -> "KVSplitPlan":
+        """One work-balanced key range per rank (``kv_split_ranges``)."""
+        ch = tuple(tuple(kv_split_ranges(seq_len, world, r)) if causal else tuple(_even_range(seq_len, world, r))
+                   for r in range(world))
+        return cls(seq_len, seq_len, world, ch, causal)
+
+    @classmethod
+    def zigzag(cls, seq_len: int, world: int, causal: bool = True, align: int = 128) -> "KVSplitPlan":
+        """Two chunks per rank (``zigzag_chunks``)."""
+        ch = tuple(tuple(zigzag_chunks(seq_len, world, r, align)) for r in range(world))
+        return cls(seq_len, seq_len, world, ch, causal)
+
+    @property
+    def slice_rows(self) -> int:
+        s = -(-self.q_len // self.world)
+        return -(-s // 16) * 16
+
+    def row_slice(self, rank: int) -> Tuple[int, int]:
+        lo = min(self.q_len, rank * self.slice_rows)
+        return lo, min(self.q_len, lo + self.slice_rows)
+
+    def chunk_first_row(self, key_start: int) -> int:
+        """First query row that sees key `key_start` (q_len if none)."""
+        if not self.causal:
+            return 0
+        return max(0, min(self.q_len, key_start - (self.kv_len - self.q_len)))
+
+    def first_row(self, rank: int) -> int:
+        rows = [self.chunk_first_row(a) for a, b in self.chunks[rank] if b > a]
+        return min(rows) if rows else self.q_len
 
 
-def merge_across_ranks(out: torch.Tensor, lse: torch.Tensor, group=None):
-    """Exact merge of this rank's partial (out fp32 [B, S, H, D], lse [B, H, S])
-    with every other rank's, via all-reduce MAX then one all-reduce SUM.
+def _even_range(seq_len: int, world: int, rank: int) -> List[Tuple[int, int]]:
+    a, b = shard_units(1, seq_len, world, rank)
+    return [(a, b)] if b > a else []
 
-    Every rank returns the merged (O fp32, lse).  Works on any backend
-    torch.distributed supports for these ops (NCCL on GPUs, gloo on CPU).
-    """
-    import torch.distributed as dist
 
-    m = lse.clone()
-    dist.all_reduce(m, op=dist.ReduceOp.MAX, group=group)
-    m_safe = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
-    w = torch.exp(lse - m_safe)  # [B, H, S]; 0 where this rank saw no key
-    B, S, H, D = out.shape
-    payload = torch.empty(B * S * H * D + B * H * S, dtype=torch.float32, device=out.device)
-    num = payload[: B * S * H * D].view(B, S, H, D)
-    torch.mul(out.float(), w.permute(0, 2, 1).unsqueeze(-1), out=num)
-    payload[B * S * H * D :].copy_(w.reshape(-1))
-    dist.all_reduce(payload, op=dist.ReduceOp.SUM, group=group)
-    wsum = payload[B * S * H * D :].view(B, H, S)
-    inv = torch.where(wsum > 0, 1.0 / wsum, torch.zeros_like(wsum))
-    merged = num * inv.permute(0, 2, 1).unsqueeze(-1)
-    lse_out = torch.where(wsum > 0, m_safe + torch.log(wsum), torch.full_like(m, float("-inf")))
-    return merged, lse_out
+# ---------------------------------------------------------------- KV split
+
+
+class CudaOps:
+    """The kernels of the KV split on this GPU: attention over one key chunk
+    (libllmx_attn.so's forward with kv_offset / kv_total) and the log-sum-exp
+    merge (llmx_attn_lse_merge)."""
+
+    def attend(self, o, lse, q, k, v, sm_scale, *, alibi_slopes, causal, sliding_window, kv_offset, kv_total):
+        ops.single_mha_attention_half(o, q, k, v, sm_scale, sliding_window, alibi_slopes=alibi_slopes,
+                                      causal=causal, lse=lse, kv_offset=kv_offset, kv_total=kv_total)
+
+    def merge(self, parts, out, lse_out):
+        """parts: (o [B, n, H, D], lse [B, H, n], row_lo, row_hi) with n =
+        row_hi - row_lo, rows counted in `out`'s row axis."""
+        B, S, H, D = out.shape
+        if out.dtype not in (torch.float16, torch.bfloat16):
+            raise RuntimeError("the KV-split merge takes fp16 or bf16 partials")
+        arr = (_lib.MergePart * max(1, len(parts)))()
+        for i, (o, l, lo, hi) in enumerate(parts):
+            if o.dtype != out.dtype or l.dtype != torch.float32 or o.stride(-1) != 1 or l.stride(-1) != 1:
+                raise RuntimeError("merge parts: O in the output dtype with unit head_dim stride, fp32 lse")
+            arr[i].o, arr[i].lse = o.data_ptr(), l.data_ptr()
+            arr[i].o_stride[:] = (o.stride(0), o.stride(1), o.stride(2))
+            arr[i].lse_stride[:] = (l.stride(0), l.stride(1))
+            arr[i].row_lo, arr[i].row_hi = int(lo), int(hi)
+        ost = (ctypes.c_int64 * 3)(out.stride(0), out.stride(1), out.stride(2))
+        dt = _lib.DTYPE["bf16" if out.dtype == torch.bfloat16 else "fp16"]
+        stream = ctypes.c_void_p(torch.cuda.current_stream(out.device).cuda_stream)
+        _lib.check(_lib.load().llmx_attn_lse_merge(len(parts), arr, dt, B, S, H, D, out.data_ptr(), ost,
+                                                   None if lse_out is None else lse_out.data_ptr(), stream))
+
+
+def _mark(timings, name, device):
+    if timings is not None and device.type == "cuda":
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(device))
+        timings.append((name, ev))
+
+
+def local_partial(q, k_chunks, v_chunks, plan: KVSplitPlan, rank: int, sm_scale: float, *, alibi_slopes=None,
+                  sliding_window: int = -1, backend=None):
+    """This rank's partial over its keys: (O [B, q_len - row0, H, D],
+    lse [B, H, q_len - row0], row0) for the rows row0 = plan.first_row(rank)
+    on.  Each chunk is computed for the rows that can see it (one kernel
+    launch per chunk) and several chunks are merged into one partial."""
+    be = backend or CudaOps()
+    B, Sq, H, D = q.shape
+    dev = q.device
+    mine = plan.chunks[rank]
+    if len(k_chunks) != len(mine) or len(v_chunks) != len(mine):
+        raise ValueError("one k / v chunk per key range of this rank")
+    row0 = plan.first_row(rank)
+    pieces = []
+    for (a, b), kc, vc in zip(mine, k_chunks, v_chunks):
+        if kc.shape[1] != b - a or vc.shape[1] != b - a:
+            raise ValueError("chunk length differs from the plan's key range")
+        r0 = plan.chunk_first_row(a)
+        if b <= a or r0 >= Sq:
+            continue
+        o = torch.empty(B, Sq - r0, H, D, dtype=q.dtype, device=dev)
+        l = torch.empty(B, H, Sq - r0, dtype=torch.float32, device=dev)
+        be.attend(o, l, q[:, r0:], kc, vc, sm_scale, alibi_slopes=alibi_slopes, causal=plan.causal,
+                  sliding_window=sliding_window, kv_offset=a, kv_total=plan.kv_len)
+        pieces.append((o, l, r0 - row0, Sq - row0))
+    if len(pieces) == 1:
+        return pieces[0][0], pieces[0][1], row0
+    part_o = torch.empty(B, Sq - row0, H, D, dtype=q.dtype, device=dev)
+    part_l = torch.empty(B, H, Sq - row0, dtype=torch.float32, device=dev)
+    if Sq > row0:
+        be.merge(pieces, part_o, part_l)
+    return part_o, part_l, row0
+
+
+def slice_part(part_o, part_l, row0: int, plan: KVSplitPlan, src: int, dst: int):
+    """The rows of rank `src`'s partial (from ``local_partial``) that fall in
+    rank `dst`'s row slice, as (O view, lse view, row_lo, row_hi) with rows
+    counted inside the slice, or None when there are none."""
+    lo, hi = plan.row_slice(dst)
+    a = max(lo, row0, plan.first_row(src))
+    if hi <= a:
+        return None
+    return part_o[:, a - row0:hi - row0], part_l[:, :, a - row0:hi - row0], a - lo, hi - lo
+
+
+def merge_slice(parts, plan: KVSplitPlan, rank: int, like: torch.Tensor, *, rows: Optional[int] = None,
+                backend=None):
+    """Merges the partials of rank `rank`'s row slice: returns (O [B, rows, H, D],
+    lse [B, H, rows]) with rows = the slice length unless given (padding rows
+    past the slice are left unwritten)."""
+    be = backend or CudaOps()
+    B, _, H, D = like.shape
+    lo, hi = plan.row_slice(rank)
+    rows = hi - lo if rows is None else rows
+    out = torch.empty(B, rows, H, D, dtype=like.dtype, device=like.device)
+    lse = torch.empty(B, H, rows, dtype=torch.float32, device=like.device)
+    if hi > lo:
+        # the merge writes a contiguous [B, H, hi - lo] lse; a padded slice
+        # takes it through a temporary
+        l_dst = lse if rows == hi - lo else torch.empty(B, H, hi - lo, dtype=torch.float32, device=like.device)
+        be.merge(parts, out[:, :hi - lo], l_dst)
+        if l_dst is not lse:
+            lse[:, :, :hi - lo].copy_(l_dst)
+    return out, lse
 
 
 def kv_split_attention(
     q: torch.Tensor,
     k_chunks: Sequence[torch.Tensor],
     v_chunks: Sequence[torch.Tensor],
-    chunk_offsets: Sequence[int],
-    kv_total: int,
+    plan: KVSplitPlan,
     sm_scale: float,
     *,
-    alibi_slopes: Optional[torch.Tensor] = None,
-    causal: bool = True,
-    sliding_window: int = -1,
+    rank: Optional[int] = None,
     group=None,
-    out_dtype: Optional[torch.dtype] = None,
+    alibi_slopes: Optional[torch.Tensor] = None,
+    sliding_window: int = -1,
+    output: str = "sharded",
+    backend=None,
+    timings: Optional[list] = None,
 ):
-    """Attention of all of `q` ([B, S, H, D]) over the keys of every rank,
-    where this rank holds the key chunks `k_chunks` / `v_chunks`
-    ([B, n_c, H_kv, D]) starting at global positions `chunk_offsets`.
+    """Attention of all of `q` ([B, q_len, H, D]) over the keys of every rank
+    of `group`, where this rank holds the key chunks `k_chunks` / `v_chunks`
+    ([B, n_c, H_kv, D]) at the global positions plan.chunks[rank].
 
-    Runs the kernel once per local chunk and merges every chunk of every
-    rank of `group` exactly (cross-rank steps skipped when torch.distributed
-    is not initialised or the group has one rank) with the library's merge
-    kernels.  Returns (O in `out_dtype` (default q's), lse fp32 [B, H, S]) on
-    every rank.
+    output="sharded": returns (O [B, hi - lo, H, D], lse [B, H, hi - lo],
+    (lo, hi)) for this rank's row slice plan.row_slice(rank);
+    output="replicated": returns (O [B, q_len, H, D], lse [B, H, q_len],
+    (0, q_len)) on every rank.  Without torch.distributed (or with one rank)
+    the plan must have one rank.  `backend` supplies attend / merge (default
+    the CUDA kernels); `timings`, if a list, receives (phase, CUDA event)
+    marks after the attention, exchange, merge and gather phases.
     """
     import torch.distributed as dist
 
-    B, S, H, D = q.shape
-    outs, lses = [], []
-    for kc, vc, off in zip(k_chunks, v_chunks, chunk_offsets):
-        o = torch.empty_like(q)
-        l = torch.empty(B, H, S, dtype=torch.float32, device=q.device)
-        ops.single_mha_attention_half(o, q, kc, vc, sm_scale, sliding_window, alibi_slopes=alibi_slopes,
-                                      causal=causal, lse=l, kv_offset=int(off), kv_total=int(kv_total))
-        outs.append(o)
-        lses.append(l)
+    if output not in ("sharded", "replicated"):
+        raise ValueError("output must be 'sharded' or 'replicated'")
     multi = dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
-    return _merge_cuda(outs, lses, q, multi, group, out_dtype)
-
-
-def _merge_cuda(outs, lses, q, multi, group, out_dtype):
-    """The merge on the GPU: row max of lse over every shard (all-reduce MAX),
-    one scale kernel writing [num | wsum] for the local partials, one
-    all-reduce SUM of that buffer, one finish kernel.  With one partial per
-    rank and at most three ranks the partials are all-gathered instead and
-    merged locally (no MAX / SUM all-reduce)."""
-    import ctypes
-
-    import torch.distributed as dist
-
-    from . import _lib
-
-    B, S, H, D = q.shape
-    if q.dtype not in (torch.float16, torch.bfloat16):
-        raise RuntimeError("the KV-split merge takes fp16 or bf16 partials")
     world = dist.get_world_size(group) if multi else 1
-    if multi and world <= 3 and len(outs) == 1:
-        # One partial per rank and few ranks: gathering every rank's 16-bit O
-        # and fp32 lse moves (world - 1) x (2 D + 4) bytes per row into each
-        # rank, against 2 (world - 1) / world x (4 D + 4) for the all-reduce
-        # of the fp32 [num | wsum] buffer; the merge then runs locally over
-        # all partials, in the same fp32 arithmetic.
-        o_all = torch.empty((world,) + tuple(q.shape), dtype=q.dtype, device=q.device)
-        l_all = torch.empty((world, B, H, S), dtype=torch.float32, device=q.device)
-        dist.all_gather_into_tensor(o_all, outs[0].contiguous(), group=group)
-        dist.all_gather_into_tensor(l_all, lses[0].contiguous(), group=group)
-        outs, lses, multi = list(o_all.unbind(0)), list(l_all.unbind(0)), False
-    if lses:
-        m = torch.stack(list(lses), 0).amax(0)
-    else:
-        m = torch.full((B, H, S), float("-inf"), device=q.device)
+    if rank is None:
+        rank = dist.get_rank(group) if multi else 0
+    if plan.world != world:
+        raise ValueError(f"the plan is for {plan.world} ranks, the group has {world}")
+    B, Sq, H, D = q.shape
+    if Sq != plan.q_len:
+        raise ValueError("q's length differs from the plan's")
+    dev = q.device
+
+    # 1. This rank's partial over its keys, rows [row0, Sq).
+    part_o, part_l, row0 = local_partial(q, k_chunks, v_chunks, plan, rank, sm_scale, alibi_slopes=alibi_slopes,
+                                         sliding_window=sliding_window, backend=backend)
+    _mark(timings, "attention", dev)
+
+    # 2. Row-slice exchange: the rows of my partial in peer p's slice go to p;
+    # the sizes come from the plan, so every pair of ranks agrees on them.
+    lo, hi = plan.row_slice(rank)
+    parts = []
+    p2p = []
+    for peer in range(world):
+        if peer == rank:
+            mine = slice_part(part_o, part_l, row0, plan, rank, rank)
+            if mine is not None:
+                parts.append(mine)
+            continue
+        out_part = slice_part(part_o, part_l, row0, plan, rank, peer)
+        if out_part is not None:
+            so, sl = out_part[0], out_part[1]
+            so = so if so.is_contiguous() else so.contiguous()
+            p2p += [dist.P2POp(dist.isend, so, peer, group), dist.P2POp(dist.isend, sl.contiguous(), peer, group)]
+        r_lo = max(lo, plan.first_row(peer))  # the peer holds rows [r_lo, hi) of my slice
+        if hi > r_lo:
+            ro = torch.empty(B, hi - r_lo, H, D, dtype=q.dtype, device=dev)
+            rl = torch.empty(B, H, hi - r_lo, dtype=torch.float32, device=dev)
+            p2p += [dist.P2POp(dist.irecv, ro, peer, group), dist.P2POp(dist.irecv, rl, peer, group)]
+            parts.append((ro, rl, r_lo - lo, hi - lo))
+    if p2p:
+        for req in dist.batch_isend_irecv(p2p):
+            req.wait()
+    _mark(timings, "exchange", dev)
+
+    # 3. Merge of my slice (padded to slice_rows for the all-gather).
+    out, lse = merge_slice(parts, plan, rank, q, rows=plan.slice_rows if output == "replicated" else None,
+                           backend=backend)
+    _mark(timings, "merge", dev)
+    if output == "sharded":
+        return out, lse, (lo, hi)
+
+    # 4. All-gather of the slices.
+    rows = plan.slice_rows
     if multi:
-        dist.all_reduce(m, op=dist.ReduceOp.MAX, group=group)
-    n = B * S * H * D
-    payload = torch.empty(n + B * H * S, dtype=torch.float32, device=q.device)
-    num, wsum = payload[:n], payload[n:]
-    lib = _lib.load()
-    stream = ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)
-    dt = _lib.DTYPE["bf16" if q.dtype == torch.bfloat16 else "fp16"]
-    outs = [o.contiguous() for o in outs]
-    optrs = (ctypes.c_void_p * max(1, len(outs)))(*[o.data_ptr() for o in outs])
-    lptrs = (ctypes.c_void_p * max(1, len(lses)))(*[l.data_ptr() for l in lses])
-    _lib.check(lib.llmx_attn_lse_merge_scale(len(outs), optrs, lptrs, m.data_ptr(), dt, B, S, H, D,
-                                             num.data_ptr(), wsum.data_ptr(), stream))
-    if multi:
-        dist.all_reduce(payload, op=dist.ReduceOp.SUM, group=group)
-    out = torch.empty(B, S, H, D, dtype=out_dtype or q.dtype, device=q.device)
-    if out.dtype != q.dtype:
-        tmp = torch.empty_like(q)
+        # concatenated along the batch axis (the layout every backend takes)
+        go = torch.empty((world * B,) + tuple(out.shape[1:]), dtype=out.dtype, device=dev)
+        gl = torch.empty((world * B,) + tuple(lse.shape[1:]), dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(go, out, group=group)
+        dist.all_gather_into_tensor(gl, lse, group=group)
+        go, gl = go.view((world,) + tuple(out.shape)), gl.view((world,) + tuple(lse.shape))
     else:
-        tmp = out
-    lse = torch.empty(B, H, S, dtype=torch.float32, device=q.device)
-    _lib.check(lib.llmx_attn_lse_merge_finish(num.data_ptr(), wsum.data_ptr(), m.data_ptr(), dt, B, S, H, D,
-                                              tmp.data_ptr(), lse.data_ptr(), stream))
-    if tmp is not out:
-        out.copy_(tmp)
-    return out, lse
+        go, gl = out.unsqueeze(0), lse.unsqueeze(0)
+    full = go.permute(1, 0, 2, 3, 4).reshape(B, world * rows, H, D)[:, :Sq]
+    full_l = gl.permute(1, 2, 0, 3).reshape(B, H, world * rows)[:, :, :Sq].contiguous()
+    _mark(timings, "gather", dev)
+    return full, full_l, (0, Sq)

@@ -47,6 +47,7 @@ import torch
 __all__ = [
     "alibi_slopes",
     "attention_ref",
+    "attention_ref_chunked",
     "attention_ref_padded",
 ]
 
@@ -195,3 +196,62 @@ def attention_ref_padded(
             out[b, :ql, h] = o_bh[:, 0]
             lse[b, h, :ql] = l_bh[0]
     return (out, lse) if return_lse else out
+
+
+def attention_ref_chunked(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    sm_scale: Optional[float] = None,
+    alibi: Optional[torch.Tensor] = None,
+    causal: bool = True,
+    rows: Optional[tuple] = None,
+    heads: Optional[Sequence[int]] = None,
+    max_elems: int = 1 << 28,
+):
+    """Whole-batch fp32 oracle on whatever device q lives on, in query-row
+    blocks, so that full-size workloads (e.g. 32768 x 32768 scores per head)
+    can be checked completely on a GPU.
+
+    q: [B, Sq, H, D]; k, v: [B, Skv, Hkv, D] (all rows valid, no padding).
+    The arithmetic is ``attention_ref``'s (fp32 scores, ALiBi + slope * j,
+    bottom-right causal mask, softmax, P V) evaluated on row blocks of at most
+    ``max_elems`` scores.  ``rows`` = (r0, r1) restricts the query rows and
+    ``heads`` the heads.  Returns (O fp32 [B, r1 - r0, len(heads), D],
+    lse fp32 [B, len(heads), r1 - r0]).
+    """
+    B, Sq, H, D = q.shape
+    Skv, Hkv = k.shape[1], k.shape[2]
+    group = H // Hkv
+    dev = q.device
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    r0, r1 = (0, Sq) if rows is None else rows
+    heads = list(range(H)) if heads is None else list(heads)
+    out = torch.empty(B, r1 - r0, len(heads), D, dtype=torch.float32, device=dev)
+    lse = torch.empty(B, len(heads), r1 - r0, dtype=torch.float32, device=dev)
+    blk = max(1, min(r1 - r0, max_elems // max(1, Skv)))
+    j = torch.arange(Skv, device=dev, dtype=torch.float32)
+    for b in range(B):
+        for hi, h in enumerate(heads):
+            kf = k[b, :, h // group].float()  # [Skv, D]
+            vf = v[b, :, h // group].float()
+            for a in range(r0, r1, blk):
+                e = min(r1, a + blk)
+                qf = q[b, a:e, h].float()  # [n, D]
+                s = (qf @ kf.t()) * sm_scale
+                if alibi is not None:
+                    s = s + float(alibi[h]) * j.view(1, Skv)
+                if causal:
+                    i = torch.arange(a, e, device=dev).view(-1, 1)
+                    s = s.masked_fill(j.view(1, Skv) > (i + (Skv - Sq)), float("-inf"))
+                m = s.amax(dim=-1, keepdim=True)
+                m = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+                p = torch.exp(s - m)
+                l = p.sum(dim=-1, keepdim=True)
+                l_safe = torch.where(l > 0, l, torch.ones_like(l))
+                out[b, a - r0:e - r0, hi] = (p @ vf) / l_safe * (l > 0)
+                lse[b, hi, a - r0:e - r0] = torch.where(l > 0, m + torch.log(l_safe),
+                                                         torch.full_like(l, float("-inf"))).squeeze(-1)
+    return out, lse

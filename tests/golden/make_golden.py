@@ -1,8 +1,10 @@
 """Generate the golden attention fixtures from the reference's own oracle.
 
-Run in a checkout where the reference source is mounted:
+Run where the reference source is available, naming its root (the
+directory holding ``csrc/test_attention.py``) as the one argument or in
+LLMX_REFERENCE_ROOT:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference-root>
 
 It reads ``ref_attention`` out of ``csrc/test_attention.py`` (lines 41-93)
 with ``ast`` -- importing that module would start its torch JIT build
@@ -76,7 +78,9 @@ def checksum(t: torch.Tensor) -> float:
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLMX_REFERENCE_ROOT")
+    if not ref_root:
+        sys.exit("usage: make_golden.py <reference-root>  (or set LLMX_REFERENCE_ROOT)")
     torch.set_grad_enabled(False)
     ref_attention = load_ref_attention(ref_root)
     arrays, manifest = {}, []

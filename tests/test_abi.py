@@ -151,4 +151,4 @@ def test_status_strings():
     lib = _lib.load()
     for code in _lib.STATUS_NAMES:
         assert lib.llmx_status_string(code)
-    assert lib.llmx_attn_abi_version() == 2
+    assert lib.llmx_attn_abi_version() == 3

@@ -1,7 +1,8 @@
-"""Multi-GPU host logic on CPU: unit sharding, zig-zag key chunks and the
-exact log-sum-exp merge, including the cross-rank merge run by two `gloo`
-ranks.  Partials come from the CPU oracle (the checker); the code under test
-is llmx_b200.parallel's partitioning and merge."""
+"""Multi-GPU host logic on CPU: unit / head / key sharding, the KV-split plan,
+and the KV-split exchange run by 2 and 4 `gloo` ranks.  The attention
+partials and the merge come from the CPU oracle (the checker, standing in for
+the kernels); the code under test is llmx_b200.parallel's partitioning, its
+row-restricted partials and its point-to-point row-slice exchange."""
 import os
 
 import pytest
@@ -62,17 +63,48 @@ def test_kv_split_ranges_cover_every_key_once(world):
     assert covered == list(range(S))
 
 
-def test_merge_of_causal_key_ranges_equals_full_attention():
-    g = torch.Generator().manual_seed(2)
-    S, H, D = 333, 2, 32
-    q, k, v = (torch.randn(1, S, H, D, generator=g) for _ in range(3))
-    a = oracle.alibi_slopes(H)
-    full, lfull = oracle.attention_ref(q[0], k[0], v[0], alibi=a, return_lse=True)
-    chunks = [parallel.causal_key_range(S, 4, r) for r in range(4)]
-    outs, lses = _partials(q, k, v, chunks, a, S)
-    out, lse = parallel.merge_partials(outs, lses)
-    torch.testing.assert_close(out[0], full, atol=2e-6, rtol=0)
-    torch.testing.assert_close(lse[0], lfull, atol=2e-6, rtol=0)
+@pytest.mark.parametrize("S,world", [(33, 3), (48, 3), (100, 8), (128, 8), (20, 2), (16, 2), (32, 2)])
+def test_causal_key_range_gives_every_rank_a_block_when_possible(S, world):
+    ranges = [parallel.causal_key_range(S, world, r) for r in range(world)]
+    covered = sorted(j for a, b in ranges for j in range(a, b))
+    assert covered == list(range(S))
+    if S >= world * 16:
+        assert all(b - a >= 16 for a, b in ranges), ranges
+    else:
+        # too short for a block per rank: the first ceil(S / 16) ranks take one each
+        assert sum(1 for a, b in ranges if b > a) == -(-S // 16)
+
+
+@pytest.mark.parametrize("start,end,heads", [(0, 256, 32), (32, 64, 32), (5, 70, 32), (3, 9, 4), (0, 1, 1),
+                                             (10, 10, 4)])
+def test_unit_runs_cover_the_range(start, end, heads):
+    runs = parallel.unit_runs(start, end, heads)
+    assert len(runs) <= 3
+    units = [b * heads + h for b0, b1, h0, h1 in runs for b in range(b0, b1) for h in range(h0, h1)]
+    assert units == list(range(start, end))
+
+
+@pytest.mark.parametrize("H,world,group", [(32, 8, 1), (32, 2, 1), (32, 8, 4), (12, 5, 3), (32, 3, 8)])
+def test_head_range_deals_whole_groups(H, world, group):
+    rs = [parallel.head_range(H, world, r, group) for r in range(world)]
+    assert rs[0][0] == 0 and rs[-1][1] == H
+    for (a0, b0), (a1, b1) in zip(rs, rs[1:]):
+        assert b0 == a1
+    assert all(a % group == 0 and b % group == 0 for a, b in rs)
+
+
+@pytest.mark.parametrize("make", ["contiguous", "zigzag"])
+@pytest.mark.parametrize("S,world", [(32768, 8), (32768, 2), (300, 2), (20, 2), (333, 4), (20, 3)])
+def test_kv_split_plan_rows_and_keys(make, S, world):
+    plan = getattr(parallel.KVSplitPlan, make)(S, world)
+    keys = sorted(j for r in range(world) for a, b in plan.chunks[r] for j in range(a, b))
+    assert keys == list(range(S))
+    rows = sorted(i for r in range(world) for i in range(*plan.row_slice(r)))
+    assert rows == list(range(S))
+    for r in range(world):
+        ks = [a for a, b in plan.chunks[r] if b > a]
+        # causal, q_len == kv_len: row i sees key a iff i >= a
+        assert plan.first_row(r) == (min(ks) if ks else S)
 
 
 def _partials(q, k, v, chunks, alibi, S):
@@ -85,45 +117,85 @@ def _partials(q, k, v, chunks, alibi, S):
     return outs, lses
 
 
-def test_merge_partials_equals_full_attention():
-    g = torch.Generator().manual_seed(0)
-    S, H, D = 300, 2, 32
+def test_merge_of_causal_key_ranges_equals_full_attention():
+    g = torch.Generator().manual_seed(2)
+    S, H, D = 333, 2, 32
     q, k, v = (torch.randn(1, S, H, D, generator=g) for _ in range(3))
     a = oracle.alibi_slopes(H)
     full, lfull = oracle.attention_ref(q[0], k[0], v[0], alibi=a, return_lse=True)
-    chunks = [c for r in range(3) for c in parallel.zigzag_chunks(S, 3, r, align=16)]
+    chunks = [parallel.causal_key_range(S, 4, r) for r in range(4)]
     outs, lses = _partials(q, k, v, chunks, a, S)
-    out, lse = parallel.merge_partials(outs, lses)
+    out, lse = oracle.merge_partials(outs, lses)
     torch.testing.assert_close(out[0], full, atol=2e-6, rtol=0)
     torch.testing.assert_close(lse[0], lfull, atol=2e-6, rtol=0)
 
 
-def _rank(rank, world, port, S, H, D, result_path):
+class OracleOps:
+    """CPU stand-in for the kernels (parallel.CudaOps): the oracle computes
+    each chunk's partial and the merge, so the test exercises the plan, the
+    row restriction and the exchange of llmx_b200.parallel."""
+
+    def attend(self, o, lse, q, k, v, sm_scale, *, alibi_slopes, causal, sliding_window, kv_offset, kv_total):
+        for b in range(q.shape[0]):
+            ob, lb = oracle.attention_ref(q[b], k[b], v[b], sm_scale=sm_scale, alibi=alibi_slopes, causal=causal,
+                                          sliding_window=sliding_window, return_lse=True, kv_offset=kv_offset,
+                                          kv_total=kv_total)
+            o[b] = ob
+            lse[b] = lb
+
+    def merge(self, parts, out, lse_out):
+        B, S, H, D = out.shape
+        O, L = oracle.merge_row_parts(parts, B, S, H, D)
+        out.copy_(O.to(out.dtype))
+        if lse_out is not None:
+            lse_out.copy_(L)
+
+
+def _split_inputs(S, B=1, H=2, D=16, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    return tuple(torch.randn(B, S, H, D, generator=g) for _ in range(3))
+
+
+def _kv_rank(rank, world, port, S, make, output, result_path):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
     import torch.distributed as dist
 
-    dist.init_process_group("gloo", rank=rank, world_size=world)
-    g = torch.Generator().manual_seed(1)
-    q, k, v = (torch.randn(1, S, H, D, generator=g) for _ in range(3))
-    a = oracle.alibi_slopes(H)
-    chunks = parallel.zigzag_chunks(S, world, rank, align=32)
-    outs, lses = _partials(q, k, v, chunks, a, S)
-    out, lse = parallel.merge_partials(outs, lses)
-    out, lse = parallel.merge_across_ranks(out, lse)
-    if rank == 0:
-        torch.save({"out": out, "lse": lse}, result_path)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    B = 2 if S == 333 else 1
+    q, k, v = _split_inputs(S, B=B)
+    plan = getattr(parallel.KVSplitPlan, make)(S, world)
+    mine = plan.chunks[rank]
+    out, lse, (lo, hi) = parallel.kv_split_attention(
+        q, [k[:, a:b] for a, b in mine], [v[:, a:b] for a, b in mine], plan, 16 ** -0.5,
+        alibi_slopes=oracle.alibi_slopes(2), output=output, backend=OracleOps())
+    torch.save({"out": out, "lse": lse, "rows": (lo, hi)}, f"{result_path}.{rank}")
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_merge_across_two_gloo_ranks(tmp_path):
-    S, H, D = 256, 2, 16
-    path = str(tmp_path / "merged.pt")
-    port = 29500 + os.getpid() % 1000
-    mp.spawn(_rank, args=(2, port, S, H, D, path), nprocs=2, join=True)
-    res = torch.load(path)
-    g = torch.Generator().manual_seed(1)
-    q, k, v = (torch.randn(1, S, H, D, generator=g) for _ in range(3))
-    full, lfull = oracle.attention_ref(q[0], k[0], v[0], alibi=oracle.alibi_slopes(H), return_lse=True)
-    torch.testing.assert_close(res["out"][0], full, atol=2e-6, rtol=0)
-    torch.testing.assert_close(res["lse"][0], lfull, atol=2e-6, rtol=0)
+@pytest.mark.parametrize("world,S,make,output", [
+    (2, 20, "contiguous", "sharded"),    # short: rank 1 holds no keys
+    (2, 300, "zigzag", "sharded"),       # rank 0 keeps one chunk, rank 1 two
+    (2, 300, "contiguous", "replicated"),
+    (4, 333, "contiguous", "sharded"),   # batch 2
+    (4, 333, "zigzag", "replicated"),
+    (4, 40, "contiguous", "replicated"),  # ranks 3 has no keys, some slices empty
+])
+def test_kv_split_exchange_over_gloo_ranks(tmp_path, world, S, make, output):
+    path = str(tmp_path / "kv")
+    port = 29500 + (os.getpid() * 7 + world * 31 + S) % 2000
+    mp.spawn(_kv_rank, args=(world, port, S, make, output, path), nprocs=world, join=True)
+    B = 2 if S == 333 else 1
+    q, k, v = _split_inputs(S, B=B)
+    a = oracle.alibi_slopes(2)
+    for r in range(world):
+        res = torch.load(f"{path}.{r}")
+        lo, hi = res["rows"]
+        if output == "replicated":
+            assert (lo, hi) == (0, S)
+        for b in range(B):
+            full, lfull = oracle.attention_ref(q[b], k[b], v[b], alibi=a, return_lse=True)
+            torch.testing.assert_close(res["out"][b], full[lo:hi], atol=2e-6, rtol=0)
+            torch.testing.assert_close(res["lse"][b], lfull[:, lo:hi], atol=2e-6, rtol=0)

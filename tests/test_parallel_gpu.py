@@ -1,11 +1,15 @@
-"""Key shards and the KV-split long-context path on the GPU.
+"""Key shards, unit / head shards and the KV-split long-context path on the GPU.
 
 * every kernel family with kv_offset / kv_total (a shard of a sequence's keys
   at its global positions) against the oracle evaluated on the same keys;
-* kv_split_attention run on one GPU over all zig-zag chunks of a virtual
-  4-rank split, against the unsplit kernel and the oracle;
-* with two or more GPUs, the real 2-rank NCCL split against one GPU's
-  unsplit result.
+* the KV split of 2, 4 and 8 virtual ranks run on one GPU (each rank's
+  row-restricted partial, the row slices each rank would receive, the merge
+  kernel), every output row against the unsplit kernel and the fp32 oracle;
+* the merge kernel against the oracle's merge (row ranges, strided views,
+  rows a part does not cover holding NaN);
+* unit and head shards against the unsplit call (bit-identical);
+* with two or more GPUs, the real 2-rank NCCL split (both plans, both output
+  forms, the short sequences where a rank holds one chunk or none).
 Tolerances: see gpu_helpers.
 """
 import os
@@ -53,24 +57,117 @@ def test_key_shard_geometry(algo, window):
     assert ql >= 1
 
 
-def test_kv_split_on_one_gpu_matches_unsplit():
+def _virtual_split(q, k, v, plan, slopes, sm_scale):
+    """Runs every virtual rank's partial, then every rank's slice merge, on
+    this GPU; returns the full output and lse assembled from the slices."""
+    B, S, H, D = q.shape
+    partials = []
+    for r in range(plan.world):
+        kc = [k[:, a:b] for a, b in plan.chunks[r]]
+        vc = [v[:, a:b] for a, b in plan.chunks[r]]
+        partials.append(parallel.local_partial(q, kc, vc, plan, r, sm_scale, alibi_slopes=slopes))
+    out = torch.empty_like(q)
+    lse = torch.empty(B, H, S, device=q.device)
+    for dst in range(plan.world):
+        parts = [p for p in (parallel.slice_part(o, l, r0, plan, src, dst)
+                             for src, (o, l, r0) in enumerate(partials)) if p is not None]
+        lo, hi = plan.row_slice(dst)
+        o, l = parallel.merge_slice(parts, plan, dst, q)
+        out[:, lo:hi] = o
+        lse[:, :, lo:hi] = l
+    return out, lse
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("make", ["contiguous", "zigzag"])
+def test_kv_split_virtual_ranks_every_row(world, make):
     S, H, D = 4096, 4, 128
     q, k, v = (rand(1, S, H, D, seed=s).cuda() for s in range(3))
     slopes = oracle.alibi_slopes(H).cuda()
     full = torch.empty_like(q)
-    llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, alibi_slopes=slopes)
-    chunks = [c for r in range(4) for c in parallel.zigzag_chunks(S, 4, r)]
-    out, lse = parallel.kv_split_attention(q, [k[:, a:b] for a, b in chunks], [v[:, a:b] for a, b in chunks],
-                                           [a for a, _ in chunks], S, D ** -0.5, alibi_slopes=slopes)
+    lfull = torch.empty(1, H, S, device="cuda")
+    llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, alibi_slopes=slopes, lse=lfull)
+    plan = getattr(parallel.KVSplitPlan, make)(S, world)
+    out, lse = _virtual_split(q, k, v, plan, slopes, D ** -0.5)
     torch.cuda.synchronize()
     assert (out.float() - full.float()).abs().max().item() <= 2e-2
-    rows = slice(S - 256, S)
-    ref = oracle.attention_ref(q[0, rows].float().cpu(), k[0].float().cpu(), v[0].float().cpu(),
-                               alibi=slopes.cpu(), causal=True)
-    assert_close(out[0, rows], ref, torch.bfloat16, "kv split rows")
+    torch.testing.assert_close(lse, lfull, atol=1e-3, rtol=0)
+    ref, lref = oracle.attention_ref_chunked(q, k, v, alibi=slopes)
+    assert_close(out, ref, torch.bfloat16, f"kv split {make}/{world}")
+    torch.testing.assert_close(lse, lref, atol=2e-3, rtol=0)
 
 
-def _nccl_rank(rank, world, port, S, H, D, path, split):
+def test_kv_split_one_rank_api():
+    S, H, D = 2048, 4, 128
+    q, k, v = (rand(1, S, H, D, seed=s).cuda() for s in range(3))
+    slopes = oracle.alibi_slopes(H).cuda()
+    full = torch.empty_like(q)
+    llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, alibi_slopes=slopes)
+    plan = parallel.KVSplitPlan.zigzag(S, 1)  # two chunks on the one rank: the local merge
+    for output in ("sharded", "replicated"):
+        out, lse, rows = parallel.kv_split_attention(q, [k[:, a:b] for a, b in plan.chunks[0]],
+                                                     [v[:, a:b] for a, b in plan.chunks[0]], plan, D ** -0.5,
+                                                     alibi_slopes=slopes, output=output)
+        torch.cuda.synchronize()
+        assert rows == (0, S)
+        assert (out.float() - full.float()).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n_parts,S,H,D", [(1, 96, 3, 64), (3, 300, 2, 128), (8, 257, 2, 128), (16, 64, 1, 256),
+                                           (2, 40, 5, 8), (0, 33, 2, 64)])
+def test_merge_kernel_matches_oracle(dtype, n_parts, S, H, D):
+    g = torch.Generator().manual_seed(n_parts * 7 + S)
+    B = 2
+    parts, cpu_parts = [], []
+    for c in range(n_parts):
+        lo = int(torch.randint(0, S // 2, (1,), generator=g))
+        hi = int(torch.randint(lo, S + 1, (1,), generator=g)) if c else S
+        n = hi - lo
+        # a strided view: every other row of a larger buffer
+        big = torch.randn(B, 2 * n + 1, H, D, generator=g).to(dtype)
+        lse = torch.randn(B, H, n, generator=g) * 3
+        if n > 2:
+            lse[:, :, 1] = float("-inf")  # a row this part never saw...
+            big[:, 2] = float("nan")       # ...whose O must not be read
+        o_dev = big.cuda()[:, ::2][:, :n]  # a strided view on the device
+        parts.append((o_dev, lse.cuda(), lo, hi))
+        cpu_parts.append((big[:, ::2][:, :n].float().nan_to_num(0.0), lse, lo, hi))
+    out = torch.full((B, S, H, D), float("nan"), dtype=dtype, device="cuda")
+    lse_out = torch.empty(B, H, S, device="cuda")
+    parallel.CudaOps().merge(parts, out, lse_out)
+    torch.cuda.synchronize()
+    ref, lref = oracle.merge_row_parts(cpu_parts, B, S, H, D)
+    assert torch.isfinite(out.float()).all()
+    assert (out.float().cpu() - ref).abs().max().item() <= 2e-2
+    fin = torch.isfinite(lref)
+    assert torch.equal(torch.isfinite(lse_out.cpu()), fin)
+    torch.testing.assert_close(lse_out.cpu()[fin], lref[fin], atol=1e-4, rtol=0)
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_unit_and_head_shards_match_the_whole_call(world):
+    B, S, H, D = 3, 512, 8, 128
+    q, k, v = (rand(B, S, H, D, seed=s).cuda() for s in range(3))
+    slopes = oracle.alibi_slopes(H).cuda()
+    full = torch.empty_like(q)
+    llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, alibi_slopes=slopes)
+    out = torch.full_like(q, float("nan"))
+    for r in range(world):
+        s, e = parallel.shard_units(B, H, world, r)
+        parallel.run_units(out, q, k, v, s, e, D ** -0.5, alibi_slopes=slopes)
+    torch.cuda.synchronize()
+    assert torch.equal(out, full)
+    out2 = torch.full_like(q, float("nan"))
+    for r in range(world):
+        h0, h1 = parallel.head_range(H, world, r)
+        llmx_b200.single_mha_attention_half(out2[:, :, h0:h1], q[:, :, h0:h1], k[:, :, h0:h1], v[:, :, h0:h1],
+                                            D ** -0.5, alibi_slopes=slopes[h0:h1])
+    torch.cuda.synchronize()
+    assert torch.equal(out2, full)
+
+
+def _nccl_rank(rank, world, port, S, H, D, path, make, output):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
 
@@ -81,55 +178,32 @@ def _nccl_rank(rank, world, port, S, H, D, path, split):
                             device_id=torch.device("cuda", rank))
     q, k, v = (rand(1, S, H, D, seed=s).cuda() for s in range(3))
     slopes = oracle.alibi_slopes(H).cuda()
-    # zig-zag: two partials per rank, merged by all-reduce; ranges: one
-    # partial per rank, merged after an all-gather.
-    chunks = parallel.zigzag_chunks(S, world, rank) if split == "zigzag" else parallel.kv_split_ranges(S, world, rank)
-    out, lse = parallel.kv_split_attention(q, [k[:, a:b] for a, b in chunks], [v[:, a:b] for a, b in chunks],
-                                           [a for a, _ in chunks], S, D ** -0.5, alibi_slopes=slopes)
+    plan = getattr(parallel.KVSplitPlan, make)(S, world)
+    mine = plan.chunks[rank]
+    out, lse, rows = parallel.kv_split_attention(q, [k[:, a:b] for a, b in mine], [v[:, a:b] for a, b in mine],
+                                                 plan, D ** -0.5, alibi_slopes=slopes, output=output)
     torch.cuda.synchronize()
-    if rank == 0:
-        torch.save({"out": out.cpu(), "lse": lse.cpu()}, path)
+    torch.save({"out": out.cpu(), "lse": lse.cpu(), "rows": rows}, f"{path}.{rank}")
     dist.barrier()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("split", ["zigzag", "ranges"])
-def test_kv_split_two_gpus_nccl(tmp_path, split):
-    S, H, D = 8192, 4, 128
-    path = str(tmp_path / "split.pt")
-    port = 29600 + os.getpid() % 1000 + (7 if split == "ranges" else 0)
-    mp.spawn(_nccl_rank, args=(2, port, S, H, D, path, split), nprocs=2, join=True)
-    res = torch.load(path)
+@pytest.mark.parametrize("S,make,output", [(8192, "zigzag", "sharded"), (8192, "contiguous", "replicated"),
+                                           (20, "contiguous", "sharded"), (300, "zigzag", "replicated")])
+def test_kv_split_two_gpus_nccl(tmp_path, S, make, output):
+    H, D = 4, 128
+    path = str(tmp_path / "split")
+    port = 29600 + (os.getpid() * 7 + S + len(make) + len(output)) % 1000
+    mp.spawn(_nccl_rank, args=(2, port, S, H, D, path, make, output), nprocs=2, join=True)
     q, k, v = (rand(1, S, H, D, seed=s).cuda() for s in range(3))
     full = torch.empty_like(q)
     lse = torch.empty(1, H, S, device="cuda")
     llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, alibi_slopes=oracle.alibi_slopes(H).cuda(),
                                         lse=lse)
     torch.cuda.synchronize()
-    assert (res["out"].float() - full.float().cpu()).abs().max().item() <= 2e-2
-    torch.testing.assert_close(res["lse"], lse.cpu(), atol=1e-3, rtol=0)
-
-
-# Shapes: full and partial row runs of a block (a block takes 1024 / (D / 8)
-# rows, at most 128), head dims from one 16-byte unit per row to 256 units.
-@pytest.mark.parametrize("n_parts,shape,dtype", [
-    (1, (2, 96, 3, 64), torch.bfloat16), (2, (2, 96, 3, 64), torch.bfloat16), (3, (2, 96, 3, 64), torch.bfloat16),
-    (8, (2, 96, 3, 64), torch.bfloat16), (2, (1, 300, 2, 128), torch.float16), (3, (3, 17, 5, 8), torch.bfloat16),
-    (2, (1, 40, 2, 72), torch.float16), (2, (1, 9, 1, 2048), torch.bfloat16)])
-def test_merge_kernels_match_torch_merge(n_parts, shape, dtype):
-    B, S, H, D = shape
-    g = torch.Generator().manual_seed(n_parts)
-    outs = [torch.randn(B, S, H, D, generator=g).to(dtype).cuda() for _ in range(n_parts)]
-    lses = [torch.randn(B, H, S, generator=g).cuda() * 3 for _ in range(n_parts)]
-    lses[0][:, :, :5] = float("-inf")  # rows the first shard never saw
-    if n_parts == 1:
-        lses[0][0, 0, 7] = float("-inf")  # a row nobody saw
-    q = torch.empty(B, S, H, D, dtype=dtype, device="cuda")
-    out, lse = parallel._merge_cuda(outs, lses, q, False, None, None)
-    ref, lref = parallel.merge_partials([o.cpu() for o in outs], [l.cpu() for l in lses])
-    torch.cuda.synchronize()
-    assert (out.float().cpu() - ref).abs().max().item() <= 2e-2
-    fin = torch.isfinite(lref)
-    assert torch.equal(torch.isfinite(lse.cpu()), fin)
-    torch.testing.assert_close(lse.cpu()[fin], lref[fin], atol=1e-4, rtol=0)
+    for r in range(2):
+        res = torch.load(f"{path}.{r}")
+        lo, hi = res["rows"]
+        assert (res["out"].float() - full[:, lo:hi].float().cpu()).abs().max().item() <= 2e-2
+        torch.testing.assert_close(res["lse"], lse[:, :, lo:hi].cpu(), atol=1e-3, rtol=0)

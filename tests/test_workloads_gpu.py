@@ -1,11 +1,13 @@
-"""The five measured workloads at full size, against the CPU oracle.
+"""The five measured workloads at full size, against the oracle.
 
 Each workload runs at its full size through the torch binding with the kernel
-family AUTO selects (the one the benchmark times).  The oracle checks the
-whole output where it finishes in seconds, and a seeded subset of (batch,
-head) units or query blocks where it would take minutes; size-independent
-properties (split-KV invariance, determinism, lse consistency) cover the
-rest.  Tolerances: see gpu_helpers.
+family AUTO selects (the one the benchmark times).  The CPU oracle checks the
+whole output where it finishes in seconds and a seeded subset of (batch,
+head) units or query blocks where it would take minutes; the same oracle
+arithmetic evaluated in fp32 on the GPU (oracle.attention_ref_chunked) checks
+every unit of the Llama-shaped prefill and every head of the long prefill.
+Size-independent properties (split-KV invariance, determinism, lse
+consistency) cover the rest.  Tolerances: see gpu_helpers.
 """
 import random
 
@@ -142,3 +144,28 @@ def test_prefill_schedule_invariance(name):
     # the pipeline's barrier phases under different timings: repeated runs are bit-identical
     for _ in range(4):
         assert torch.equal(run(w, inp), queued)
+
+
+def test_llama_prefill_every_unit_vs_fp32_oracle_on_gpu():
+    w = WORKLOADS["llama7b_prefill_bf16_b8_h32_s2048_d128"]
+    inp = make_inputs(w, "cuda")
+    lse = torch.empty(w.batch, w.n_heads, w.q_len, device="cuda")
+    out = run(w, inp, lse=lse)
+    ref, lref = oracle.attention_ref_chunked(inp.q, inp.k, inp.v, sm_scale=w.sm_scale, causal=True)
+    assert_close(out, ref, w.dtype, "llama prefill, all 256 units")
+    torch.testing.assert_close(lse, lref, atol=2e-3, rtol=0)
+
+
+def test_long_prefill_every_head_vs_fp32_oracle_on_gpu():
+    w = WORKLOADS["long_prefill_bf16_b1_h32_s32768_d128"]
+    inp = make_inputs(w, "cuda")
+    lse = torch.empty(1, w.n_heads, w.q_len, device="cuda")
+    out = run(w, inp, lse=lse)
+    for h0 in range(0, w.n_heads, 8):
+        hs = list(range(h0, h0 + 8))
+        ref, lref = oracle.attention_ref_chunked(inp.q, inp.k, inp.v, sm_scale=w.sm_scale, alibi=inp.alibi,
+                                                 causal=True, heads=hs)
+        assert_close(out[:, :, h0:h0 + 8], ref, w.dtype, f"long prefill heads {h0}-{h0 + 7}")
+        torch.testing.assert_close(lse[:, h0:h0 + 8], lref, atol=2e-3, rtol=0)
+        del ref, lref
+    llmx_b200.device_status(0)

@@ -5,8 +5,9 @@ critical loops that cannot afford cudaMalloc's device-wide synchronisation,
 cannot hand the library a workspace.  This entry point keeps the split
 partials in a static device array instead.  The test calls it through the C
 ABI, twice in a row on different inputs (the array keeps the previous call's
-contents), and checks each result against llmx_attn_fwd given a workspace,
-within the GPU tests' tolerance (gpu_helpers).  It also checks that a request
+contents), and checks each result against llmx_attn_fwd given a workspace
+and against the fp32 CPU oracle directly, within the GPU tests' tolerance
+(gpu_helpers).  It also checks that a request
 larger than the array is refused before anything is launched.
 
 This file is collected last so that a failing run has already run every
@@ -17,6 +18,7 @@ import ctypes
 import pytest
 import torch
 
+import oracle
 from gpu_helpers import assert_close, needs_cuda
 from llmx_b200 import _lib, ops
 
@@ -52,6 +54,10 @@ def test_noalloc_decode_matches_workspace_decode_twice():
         out = _noalloc(q, k, v, lens, slopes)
         torch.cuda.synchronize()
         assert_close(out, ref, torch.bfloat16, f"no-alloc decode, call {seed + 1}")
+        direct = oracle.attention_ref_padded(q.float().cpu(), k.float().cpu(), v.float().cpu(),
+                                             kv_lens=lens.cpu().tolist(), alibi=slopes.cpu(),
+                                             sm_scale=q.shape[-1] ** -0.5)
+        assert_close(out, direct, torch.bfloat16, f"no-alloc decode vs the oracle, call {seed + 1}")
     ops.device_status(0)
 
 
