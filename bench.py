@@ -156,7 +156,7 @@ def measure_device(w, inp, steps, warmup, stream):
     return ms, out
 
 
-def measure_e2e(w, inp, steps, warmup, stream, chunks=4):
+def measure_e2e(w, inp, steps, warmup, stream, chunks=8):
     """Same workload through the public host-memory API
     (llmx_b200.HostAttention: pinned host inputs and output, the batch cut
     into `chunks` whose uploads, kernels and downloads overlap on three
@@ -167,7 +167,7 @@ def measure_e2e(w, inp, steps, warmup, stream, chunks=4):
     kh = inp.k.cpu().pin_memory()
     vh = inp.v.cpu().pin_memory()
     oh = torch.empty_like(qh).pin_memory()
-    run = llmx_b200.HostAttention(qh, kh, inp.q.device, chunks=chunks)
+    run = llmx_b200.HostAttention(qh, kh, inp.q.device, chunks=min(chunks, w.batch))
     kw = dict(alibi_slopes=inp.alibi, causal=w.causal, q_lens=inp.q_lens, kv_lens=inp.kv_lens)
     times = []
     for i in range(warmup + steps):
@@ -282,7 +282,7 @@ def bench_workload(name, steps, warmup, rank, world, device, stream, peaks, with
         res["e2e"] = {"value": work * world * n / (float(t.item()) * 1e-3) / scale, "unit": unit,
                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                       "copy_gbs": (h2d + d2h) / (e2e_ms * 1e-3) / 1e9,
-                      "pipeline": "HostAttention: batch in 4 chunks, upload / kernel / download on 3 streams"}
+                      "pipeline": "HostAttention: batch in 8 chunks, upload / kernel / download on 3 streams"}
     return res, w, inp
 
 
@@ -314,7 +314,8 @@ def check_parity(out, lse, q, k, v, w, alibi, rows, heads, unsplit, world, devic
     max_abs = float(err.max()) if err.numel() else 0.0
     mean_rel = float(err.mean() / ref.abs().mean().clamp_min(1e-12)) if err.numel() else 0.0
     fin = torch.isfinite(lref)
-    lse_err = float((lse[fin] - lref[fin]).abs().max()) if fin.any() else 0.0
+    # lse reaches ~3e4 with ALiBi (one fp32 ulp ~2e-3): error beyond 1e-6 relative
+    lse_err = float(((lse[fin] - lref[fin]).abs() - 1e-6 * lref[fin].abs()).clamp_min(0).max()) if fin.any() else 0.0
     vs_unsplit = float((out.float() - unsplit.float()).abs().max()) if out.numel() else 0.0
     rng = random.Random(seed + r0)
     cpu_err = 0.0
@@ -331,7 +332,7 @@ def check_parity(out, lse, q, k, v, w, alibi, rows, heads, unsplit, world, devic
         cpu_err = max(cpu_err, float((got - ro).abs().max()))
     worst = _max_over_ranks([max_abs, mean_rel, lse_err, vs_unsplit, cpu_err], world, device)
     ok = worst[0] <= 2e-2 and worst[1] <= 1e-2 and worst[2] <= 2e-3 and worst[4] <= 2e-2
-    return {"max_abs": worst[0], "mean_rel": worst[1], "lse_max_abs": worst[2], "vs_unsplit_max_abs": worst[3],
+    return {"max_abs": worst[0], "mean_rel": worst[1], "lse_max_abs_beyond_1e-6_rel": worst[2], "vs_unsplit_max_abs": worst[3],
             "cpu_oracle_blocks_max_abs": worst[4], "cpu_oracle_blocks_per_rank": cpu_blocks, "ok": bool(ok),
             "checked": "every row and head each rank holds vs the fp32 oracle on the GPU; the single-GPU kernel; "
                        "seeded 128-row blocks vs the CPU oracle"}

@@ -1,9 +1,11 @@
 // llmx::Tensor -- the tensor type llmx's attention op takes.
 //
 // Same public surface as the reference (include/llmx/tensor.h:17-177):
-// ScalarType, DeviceType, Device, DataPtr, Tensor with dims/strides/capacity,
-// allocate / resize / to_device, and the llmx_allocate / llmx_free /
-// llmx_copy helpers.  Differences, all internal:
+// ScalarType, DeviceType, Device and the cpu0 / cuda0..cuda7 shorthands,
+// MemInfo, DataPtr, Tensor with dims/strides/capacity, allocate / resize /
+// to_device, and the llmx_allocate / llmx_free / llmx_mem_info / llmx_copy
+// helpers, so code written against the reference header compiles unchanged.
+// Differences, all internal:
 //  * CUDA tensors live in device memory (cudaMalloc + zero fill) instead of
 //    managed memory (tensor.cpp:64-70);
 //  * ownership is a shared control block, so copies share storage and the
@@ -37,8 +39,37 @@ struct Device {
   bool operator!=(const Device &other) const { return !(*this == other); }
 };
 
+// Device shorthands of the reference header (tensor.h:38-46).
+#define cpu0 Device(DeviceType::kCPU)
+#define cuda0 Device(DeviceType::kCUDA, 0)
+#define cuda1 Device(DeviceType::kCUDA, 1)
+#define cuda2 Device(DeviceType::kCUDA, 2)
+#define cuda3 Device(DeviceType::kCUDA, 3)
+#define cuda4 Device(DeviceType::kCUDA, 4)
+#define cuda5 Device(DeviceType::kCUDA, 5)
+#define cuda6 Device(DeviceType::kCUDA, 6)
+#define cuda7 Device(DeviceType::kCUDA, 7)
+
+// What llmx_allocate recorded about a block it returned (tensor.h:48-52).
+struct MemInfo {
+  void *data;
+  std::size_t nbytes;
+  Device device;
+};
+
+// Zero-filled storage on `device` (64-byte aligned host memory, or CUDA
+// device memory), recorded so that llmx_free / llmx_mem_info find it.  The
+// record is process-wide and guarded by a mutex (the reference keeps one
+// unguarded map per translation unit, tensor.h:54-67).
 void *llmx_allocate(size_t nbytes, Device device);
+// Frees a block llmx_allocate returned; pointers it did not return are
+// ignored, as in the reference (tensor.cpp:134-146).
+void llmx_free(void *data);
+// Frees `data` as memory of `device` (also accepted for blocks the library
+// did not allocate: host memory from malloc, device memory from cudaMalloc).
 void llmx_free(void *data, Device device);
+// The record of a block llmx_allocate returned, or nullopt (tensor.cpp:148-153).
+std::optional<MemInfo> llmx_mem_info(void *data);
 void llmx_copy(Device src_device, Device dst_device, const void *src, void *dst, size_t nbytes);
 // Element-type conversion of `num` contiguous elements in device-addressable
 // memory (src/tensor.cpp:108-118), on the legacy stream like the reference's
@@ -50,7 +81,7 @@ void llmx_copy(ScalarType src_dtype, ScalarType dst_dtype, const void *src, void
 class DataPtr {
  public:
   DataPtr() = default;
-  explicit DataPtr(void *ptr) : ptr_(ptr) {}  // non-owning
+  DataPtr(void *ptr) : ptr_(ptr) {}  // non-owning
   DataPtr(void *ptr, Device device);          // owning: frees with llmx_free
 
   void *ptr() const noexcept { return ptr_; }
@@ -71,7 +102,7 @@ class DataPtr {
 class Tensor {
  public:
   Tensor() = default;
-  Tensor(const std::vector<int> &dims, ScalarType dtype, Device device);  // allocates, zeroed
+  Tensor(const std::vector<int> &dims, ScalarType dtype, Device device);  // metadata; allocate() adds storage
   Tensor(void *data, const std::vector<int> &dims, ScalarType dtype, Device device);  // wraps
 
   ScalarType dtype() const noexcept { return dtype_; }

@@ -93,6 +93,56 @@ def build(force: bool = False, verbose: bool = False, extra_flags=()) -> str:
     return LIB
 
 
+BIND_SRC = os.path.join(CSRC, "llmx_bind.cpp")
+
+
+def binding_path() -> str:
+    import sysconfig
+
+    return os.path.join(PKG, "llmx_bind" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def torch_extension_flags(module: str):
+    """Compiler and linker flags of a torch extension module named `module`
+    (what torch.utils.cpp_extension would pass, without its JIT cache)."""
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    inc = [*ce.include_paths(), os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include"),
+           sysconfig.get_paths()["include"]]
+    cflags = ["-O2", "-std=c++17", "-fPIC", "-shared", f"-DTORCH_EXTENSION_NAME={module}",
+              "-DTORCH_API_INCLUDE_EXTENSION_H", f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+              *["-I" + d for d in inc]]
+    tlib = ce.library_paths()[0]
+    ldflags = ["-L" + tlib, "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
+               "-Wl,-rpath," + tlib]
+    return cflags, ldflags
+
+
+def build_binding(force: bool = False) -> str:
+    """Builds the torch binding (csrc/llmx_bind.cpp) as the extension module
+    llmx_b200.llmx_bind, linked against libllmx_attn.so next to it."""
+    lib = build()
+    out = binding_path()
+    deps = [BIND_SRC, lib, os.path.join(INCLUDE, "llmx_attn.h")]
+    if not force and os.path.exists(out) and all(os.path.getmtime(d) <= os.path.getmtime(out) for d in deps):
+        return out
+    cflags, ldflags = torch_extension_flags("llmx_bind")
+    gxx = shutil.which("g++") or "g++"
+    tmp = out + ".tmp"
+    cmd = [gxx, *cflags, "-I" + INCLUDE, BIND_SRC, "-o", tmp, *ldflags, "-L" + PKG, "-lllmx_attn",
+           "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch binding build failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, out)
+    return out
+
+
 if __name__ == "__main__":
     args = sys.argv[1:]
     print(build(force="--force" in args, verbose="-v" in args or "--verbose" in args))
+    if "--no-binding" not in args:
+        print(build_binding(force="--force" in args))

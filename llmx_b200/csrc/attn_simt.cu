@@ -12,18 +12,21 @@
 // masks (mask.h:41-81) and ALiBi (mask.h:28-37,75-77).  Rows with no visible
 // key produce 0 instead of the reference's NaN.
 //
-// Tiling: one CTA = 16 query rows of one (batch, head); 128 threads; key
-// tiles of 64 staged in shared memory as fp32.
+// Tiling: one CTA = kBM (16, or 8 when 16-row tiles would leave SMs idle)
+// query rows of one (batch, head); 128 threads; key tiles of 64 staged in
+// shared memory as fp32.  Small problems are latency-bound, so the staging
+// of Q, K and V tiles issues a thread's 16-byte loads in batches of four
+// before converting and storing any of them (rows with 16-byte aligned
+// starts; other layouts take element loads).
 #include "common.cuh"
 
 namespace llmx_b200 {
 namespace {
 
-constexpr int kBM = 16;
 constexpr int kBN = 64;
 constexpr int kThreads = 128;
 
-template <int DMAX>
+template <int DMAX, int kBM>
 struct SimtSmem {
   static constexpr int kQ = kBM * DMAX;
   static constexpr int kK = kBN * (DMAX + 1);
@@ -32,14 +35,73 @@ struct SimtSmem {
   static constexpr size_t bytes = sizeof(float) * (kQ + kK + kV + kS + 3 * kBM);
 };
 
+// 16 bytes of T -> floats (4 for fp32, 8 for 16-bit types).
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4 &u, float *f) {
+  if constexpr (std::is_same<T, float>::value) {
+    f[0] = __uint_as_float(u.x);
+    f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z);
+    f[3] = __uint_as_float(u.w);
+  } else {
+    float g[8];
+    unpack8<T>(u, g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = g[i];
+  }
+}
+
+// Stages rows [r0, r0 + n_rows) (row r at src + r * stride, D elements) into
+// dst[(r - r0) * dst_pitch + d] as fp32; rows at or past `valid` and columns
+// past D are zero.  vec: 16-byte aligned row starts and D a multiple of the
+// 16-byte element count.
 template <typename T, int DMAX>
-__global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a) {
+__device__ __forceinline__ void stage_rows(float *dst, int dst_pitch, const T *src, long long stride, int r0,
+                                           int n_rows, int valid, int D, bool vec) {
+  constexpr int kE = 16 / sizeof(T);  // elements per 16-byte unit
+  if (vec) {
+    const int upr = DMAX / kE;  // units per staged row (columns past D read as zero)
+    const int n_units = n_rows * upr;
+    for (int base = threadIdx.x; base < n_units; base += 4 * kThreads) {
+      uint4 raw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = base + u * kThreads;
+        const int r = idx / upr, x = idx - r * upr;
+        raw[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (idx < n_units && r0 + r < valid && x * kE < D)
+          raw[u] = *reinterpret_cast<const uint4 *>(src + (long long)(r0 + r) * stride + x * kE);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = base + u * kThreads;
+        if (idx < n_units) {
+          const int r = idx / upr, x = idx - r * upr;
+          float f[kE];
+          unpack16<T>(raw[u], f);
+#pragma unroll
+          for (int i = 0; i < kE; ++i) dst[r * dst_pitch + x * kE + i] = f[i];
+        }
+      }
+    }
+  } else {
+    for (int e = threadIdx.x; e < n_rows * DMAX; e += kThreads) {
+      const int r = e / DMAX, d = e % DMAX;
+      dst[r * dst_pitch + d] = (r0 + r < valid && d < D) ? Elem<T>::to_f(src[(long long)(r0 + r) * stride + d]) : 0.f;
+    }
+  }
+}
+
+template <typename T, int DMAX, int kBM>
+__global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a, bool vec) {
+  using Sm = SimtSmem<DMAX, kBM>;
+  constexpr int kCols = kThreads / kBM;  // output column groups per row
   extern __shared__ float smem[];
   float *Qs = smem;
-  float *Ks = Qs + SimtSmem<DMAX>::kQ;
-  float *Vs = Ks + SimtSmem<DMAX>::kK;
-  float *Ss = Vs + SimtSmem<DMAX>::kV;
-  float *m_s = Ss + SimtSmem<DMAX>::kS;
+  float *Ks = Qs + Sm::kQ;
+  float *Vs = Ks + Sm::kK;
+  float *Ss = Vs + Sm::kV;
+  float *m_s = Ss + Sm::kS;
   float *l_s = m_s + kBM;
   float *alpha_s = l_s + kBM;
 
@@ -58,11 +120,7 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a) {
   const float slope = a.alibi ? a.alibi[h] : 0.f;
 
   // Q tile -> fp32 smem (rows past q_len and columns past D are zero).
-  for (int e = tid; e < kBM * DMAX; e += kThreads) {
-    const int r = e / DMAX, d = e % DMAX;
-    const int qi = q0 + r;
-    Qs[e] = (qi < ql && d < D) ? Elem<T>::to_f(qp[qi * a.qs[1] + d]) : 0.f;
-  }
+  stage_rows<T, DMAX>(Qs, DMAX, qp, a.qs[1], q0, kBM, ql, D, vec);
   if (tid < kBM) {
     m_s[tid] = -CUDART_INF_F;
     l_s[tid] = 0.f;
@@ -81,23 +139,18 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a) {
   }
   lo = (lo / kBN) * kBN;
 
-  // Output mapping: thread -> (row r_o, columns d_o + 8 i).
-  const int r_o = tid / 8;
-  const int d_o = tid % 8;
-  constexpr int kPer = DMAX / 8;
+  // Output mapping: thread -> (row r_o, columns d_o + kCols i).
+  const int r_o = tid / kCols;
+  const int d_o = tid % kCols;
+  constexpr int kPer = DMAX / kCols;
   float acc[kPer];
 #pragma unroll
   for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
   __syncthreads();
 
   for (int n0 = lo; n0 < hi; n0 += kBN) {
-    for (int e = tid; e < kBN * DMAX; e += kThreads) {
-      const int c = e / DMAX, d = e % DMAX;
-      const int j = n0 + c;
-      const bool ok = j < kl && d < D;
-      Ks[c * (DMAX + 1) + d] = ok ? Elem<T>::to_f(kp[j * a.ks[1] + d]) : 0.f;
-      Vs[c * DMAX + d] = ok ? Elem<T>::to_f(vp[j * a.vs[1] + d]) : 0.f;
-    }
+    stage_rows<T, DMAX>(Ks, DMAX + 1, kp, a.ks[1], n0, kBN, kl, D, vec);
+    stage_rows<T, DMAX>(Vs, DMAX, vp, a.vs[1], n0, kBN, kl, D, vec);
     __syncthreads();
     // Scores: 16 x 64 entries, 8 per thread, lanes along keys.
     for (int e = tid; e < kBM * kBN; e += kThreads) {
@@ -151,7 +204,7 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a) {
         const float p = pr[c];
         const float *vr = Vs + c * DMAX + d_o;
 #pragma unroll
-        for (int i = 0; i < kPer; ++i) acc[i] = fmaf(p, vr[8 * i], acc[i]);
+        for (int i = 0; i < kPer; ++i) acc[i] = fmaf(p, vr[kCols * i], acc[i]);
       }
     }
     __syncthreads();
@@ -163,7 +216,7 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a) {
     const float inv = (l > 0.f && qi < ql) ? 1.f / l : 0.f;
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
-      const int d = d_o + 8 * i;
+      const int d = d_o + kCols * i;
       if (d < D) op[qi * a.os[1] + d] = Elem<T>::from_f(acc[i] * inv);
     }
     if (a.lse != nullptr && d_o == 0) {
@@ -173,22 +226,37 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a) {
   }
 }
 
-template <typename T, int DMAX>
-cudaError_t launch_simt_t(const AttnArgs &a, cudaStream_t s) {
-  const size_t smem = SimtSmem<DMAX>::bytes;
-  auto kern = attn_simt_kernel<T, DMAX>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+template <typename T, int DMAX, int kBM>
+cudaError_t launch_simt_t(const AttnArgs &a, bool vec, cudaStream_t s) {
+  const size_t smem = SimtSmem<DMAX, kBM>::bytes;
+  auto kern = attn_simt_kernel<T, DMAX, kBM>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
   dim3 grid((a.Sq + kBM - 1) / kBM, a.H, a.B);
-  kern<<<grid, kThreads, smem, s>>>(a);
+  kern<<<grid, kThreads, smem, s>>>(a, vec);
   return cudaGetLastError();
+}
+
+// 16-row tiles, or 8-row tiles when 16-row tiles leave SMs without a CTA.
+template <typename T, int DMAX>
+cudaError_t launch_simt_m(const AttnArgs &a, bool vec, cudaStream_t s) {
+  const long long ctas16 = (long long)((a.Sq + 15) / 16) * a.H * a.B;
+  if (ctas16 < a.num_sms) return launch_simt_t<T, DMAX, 8>(a, vec, s);
+  return launch_simt_t<T, DMAX, 16>(a, vec, s);
 }
 
 template <typename T>
 cudaError_t launch_simt_d(const AttnArgs &a, cudaStream_t s) {
-  if (a.D <= 64) return launch_simt_t<T, 64>(a, s);
-  if (a.D <= 128) return launch_simt_t<T, 128>(a, s);
-  return launch_simt_t<T, 256>(a, s);
+  constexpr int kE = 16 / sizeof(T);
+  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  bool vec = al16(a.q) && al16(a.k) && al16(a.v) && a.D % kE == 0;
+  for (int i = 1; i < 3; ++i) vec = vec && a.qs[i] % kE == 0 && a.ks[i] % kE == 0 && a.vs[i] % kE == 0;
+  vec = vec && a.qs[0] % kE == 0 && a.ks[0] % kE == 0 && a.vs[0] % kE == 0;
+  if (a.D <= 64) return launch_simt_m<T, 64>(a, vec, s);
+  if (a.D <= 128) return launch_simt_m<T, 128>(a, vec, s);
+  return launch_simt_m<T, 256>(a, vec, s);
 }
 
 }  // namespace

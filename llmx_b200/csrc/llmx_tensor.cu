@@ -6,8 +6,10 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <stdexcept>
 #include <string>
+#include <unordered_map>
 
 #include "llmx/tensor.h"
 #include "llmx_attn.h"
@@ -16,6 +18,21 @@ namespace llmx {
 namespace {
 void cuda_ok(cudaError_t e, const char *what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Blocks llmx_allocate returned, for llmx_free(void *) and llmx_mem_info.
+std::mutex g_blocks_mu;
+std::unordered_map<void *, MemInfo> &blocks() {
+  static auto *m = new std::unordered_map<void *, MemInfo>();  // outlives static destructors
+  return *m;
+}
+
+void release(void *data, Device device) {
+  if (device.type == DeviceType::kCPU) {
+    std::free(data);
+  } else {
+    cudaFree(data);
+  }
 }
 }  // namespace
 
@@ -30,30 +47,55 @@ size_t get_scalar_size(ScalarType dtype) {
 
 void *llmx_allocate(size_t nbytes, Device device) {
   if (nbytes == 0) return nullptr;
+  void *p = nullptr;
   if (device.type == DeviceType::kCPU) {
-    void *p = nullptr;
     if (posix_memalign(&p, 64, nbytes) != 0) throw std::bad_alloc();
     std::memset(p, 0, nbytes);
-    return p;
+  } else {
+    int prev = 0;
+    cuda_ok(cudaGetDevice(&prev), "cudaGetDevice");
+    cuda_ok(cudaSetDevice(device.id < 0 ? 0 : device.id), "cudaSetDevice");
+    cudaError_t e = cudaMalloc(&p, nbytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, nbytes);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess && p != nullptr) {
+      cudaFree(p);
+      p = nullptr;
+    }
+    cuda_ok(e, "cudaMalloc");
   }
-  int prev = 0;
-  cuda_ok(cudaGetDevice(&prev), "cudaGetDevice");
-  cuda_ok(cudaSetDevice(device.id < 0 ? 0 : device.id), "cudaSetDevice");
-  void *p = nullptr;
-  cudaError_t e = cudaMalloc(&p, nbytes);
-  if (e == cudaSuccess) e = cudaMemset(p, 0, nbytes);
-  cudaSetDevice(prev);
-  cuda_ok(e, "cudaMalloc");
+  std::lock_guard<std::mutex> lock(g_blocks_mu);
+  blocks()[p] = MemInfo{p, nbytes, device};
   return p;
+}
+
+void llmx_free(void *data) {
+  if (data == nullptr) return;
+  Device device;
+  {
+    std::lock_guard<std::mutex> lock(g_blocks_mu);
+    auto it = blocks().find(data);
+    if (it == blocks().end()) return;
+    device = it->second.device;
+    blocks().erase(it);
+  }
+  release(data, device);
 }
 
 void llmx_free(void *data, Device device) {
   if (data == nullptr) return;
-  if (device.type == DeviceType::kCPU) {
-    std::free(data);
-  } else {
-    cudaFree(data);
+  {
+    std::lock_guard<std::mutex> lock(g_blocks_mu);
+    blocks().erase(data);
   }
+  release(data, device);
+}
+
+std::optional<MemInfo> llmx_mem_info(void *data) {
+  std::lock_guard<std::mutex> lock(g_blocks_mu);
+  auto it = blocks().find(data);
+  if (it == blocks().end()) return std::nullopt;
+  return it->second;
 }
 
 void llmx_copy(Device src_device, Device dst_device, const void *src, void *dst,
@@ -78,10 +120,11 @@ void llmx_copy(ScalarType src_dtype, ScalarType dst_dtype, const void *src, void
 DataPtr::DataPtr(void *ptr, Device device)
     : ptr_(ptr), owner_(ptr, [device](void *p) { llmx_free(p, device); }) {}
 
+// Metadata only: storage comes with allocate(), as in the reference
+// (tensor.cpp:213-217; tensor_test.cpp checks is_valid() is false here).
 Tensor::Tensor(const std::vector<int> &dims, ScalarType dtype, Device device)
     : dtype_(dtype), device_(device) {
   set_dims(dims);
-  allocate();
 }
 
 Tensor::Tensor(void *data, const std::vector<int> &dims, ScalarType dtype, Device device)

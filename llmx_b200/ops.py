@@ -134,6 +134,23 @@ def _run(p, device: torch.device, keep) -> None:
         _lib.check(lib.llmx_attn_fwd(ctypes.byref(p), ctypes.c_void_p(stream)))
 
 
+_EXT = None
+
+
+def _extension():
+    """The C++ torch binding (llmx_b200.llmx_bind, built by
+    ``python -m llmx_b200.build``), or None when it has not been built."""
+    global _EXT
+    if _EXT is None:
+        try:
+            from . import llmx_bind
+
+            _EXT = llmx_bind
+        except ImportError:
+            _EXT = False
+    return _EXT or None
+
+
 def single_mha_attention_half(
     output: torch.Tensor,
     q: torch.Tensor,
@@ -156,10 +173,26 @@ def single_mha_attention_half(
 
     ``kv_offset`` / ``kv_total`` describe a shard of a sequence's keys: local
     key j sits at global position kv_offset + j and the causal / window
-    diagonal uses the full key length kv_total (0: the local length)."""
-    p, keep = build_params(output, q, k, v, sm_scale, sliding_window, logits_soft_cap,
-                           alibi_slopes=alibi_slopes, causal=causal, q_lens=q_lens, kv_lens=kv_lens,
-                           lse=lse, algo=algo, kv_offset=kv_offset, kv_total=kv_total)
+    diagonal uses the full key length kv_total (0: the local length).
+
+    Runs through the C++ torch binding (llmx_b200.llmx_bind: the checks and
+    the C-ABI call in C++, a few microseconds of host time) when it is built,
+    else through ctypes (``single_mha_attention_half_ctypes``); both call
+    the same library entry points with the same request."""
+    ext = _extension()
+    if ext is not None:
+        ext.single_mha_attention_half(output, q, k, v, float(sm_scale), int(sliding_window), float(logits_soft_cap),
+                                      alibi_slopes=alibi_slopes, causal=bool(causal), q_lens=q_lens, kv_lens=kv_lens,
+                                      lse=lse, algo=algo, kv_offset=int(kv_offset), kv_total=int(kv_total))
+        return
+    single_mha_attention_half_ctypes(output, q, k, v, sm_scale, sliding_window, logits_soft_cap,
+                                     alibi_slopes=alibi_slopes, causal=causal, q_lens=q_lens, kv_lens=kv_lens,
+                                     lse=lse, algo=algo, kv_offset=kv_offset, kv_total=kv_total)
+
+
+def single_mha_attention_half_ctypes(output, q, k, v, sm_scale, sliding_window=-1, logits_soft_cap=0.0, **kw):
+    """The same op through ctypes over the C ABI (no compiled binding needed)."""
+    p, keep = build_params(output, q, k, v, sm_scale, sliding_window, logits_soft_cap, **kw)
     _run(p, q.device, keep)
 
 

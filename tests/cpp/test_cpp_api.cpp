@@ -40,7 +40,11 @@ static int g_fail = 0;
 static void tensor_semantics() {
   Device cpu(DeviceType::kCPU), gpu(DeviceType::kCUDA, 0);
   Tensor t({2, 3, 4}, ScalarType::kFP32, cpu);
+  EXPECT(!t.is_valid());  // construction sets metadata only (tensor_test.cpp:18-28)
+  t.allocate();
+  EXPECT(t.is_valid());
   EXPECT(t.numel() == 24 && t.capacity() == 24 && t.contiguous());
+  EXPECT(llmx_mem_info(t.data_ptr()).has_value() && llmx_mem_info(t.data_ptr())->nbytes == 96);
   EXPECT(t.stride(0) == 12 && t.stride(1) == 4 && t.stride(2) == 1 && t.count(1) == 12);
   const float *p = t.const_data_ptr<float>();
   bool zero = true;
@@ -81,8 +85,9 @@ static void smoke_zero_inputs() {
   // test/cuda/mha_attention_test.cpp: all-zero q/k/v, causal, no ALiBi.
   const int S = 256, H = 4, Hkv = 2, D = 128;
   Device gpu(DeviceType::kCUDA, 0);
-  Tensor q({S, H, D}, ScalarType::kFP16, gpu), k({S, Hkv, D}, ScalarType::kFP16, gpu),
-      v({S, Hkv, D}, ScalarType::kFP16, gpu), o({S, H, D}, ScalarType::kFP16, gpu);
+  Tensor q({S, H, D}, ScalarType::kFP16, cuda0), k({S, Hkv, D}, ScalarType::kFP16, cuda0),
+      v({S, Hkv, D}, ScalarType::kFP16, cuda0), o({S, H, D}, ScalarType::kFP16, cuda0);
+  for (Tensor *t : {&q, &k, &v, &o}) t->allocate();
   llmx_single_mha_attention(o, q, k, v, std::nullopt, 1.0f / std::sqrt(float(D)));
   EXPECT(cudaDeviceSynchronize() == cudaSuccess);
   std::vector<__half> h(o.numel());
@@ -105,6 +110,7 @@ static void known_answer_uniform_weights() {
   for (auto &x : hv) x = __float2bfloat16(rnd());
   Tensor q({S, H, D}, ScalarType::kBF16, gpu), k({S, Hkv, D}, ScalarType::kBF16, gpu),
       v({S, Hkv, D}, ScalarType::kBF16, gpu), o({S, H, D}, ScalarType::kBF16, gpu);
+  for (Tensor *t : {&q, &k, &v, &o}) t->allocate();
   llmx_copy(cpu, gpu, hq.data(), q.data_ptr(), q.nbytes());
   llmx_copy(cpu, gpu, hk.data(), k.data_ptr(), k.nbytes());
   llmx_copy(cpu, gpu, hv.data(), v.data_ptr(), v.nbytes());
@@ -133,6 +139,7 @@ static void argument_errors_throw() {
   Device gpu(DeviceType::kCUDA, 0);
   Tensor q({16, 4, 64}, ScalarType::kFP16, gpu), k({16, 3, 64}, ScalarType::kFP16, gpu),
       v({16, 3, 64}, ScalarType::kFP16, gpu), o({16, 4, 64}, ScalarType::kFP16, gpu);
+  for (Tensor *t : {&q, &k, &v, &o}) t->allocate();
   bool threw = false;
   try {
     llmx_single_mha_attention(o, q, k, v, std::nullopt, 0.125f);  // 4 heads over 3 kv heads
@@ -147,6 +154,7 @@ static void registry_conversions() {
   // ops_test.cpp: fp16 [1, 2, 3, 4] -> fp32.  The input starts on the host;
   // the executor moves it to the device.
   Tensor input({4}, ScalarType::kFP16, cpu);
+  input.allocate();
   for (int i = 0; i < 4; ++i) input.data_ptr<__half>()[i] = __float2half(float(i + 1));
   Tensor output;
   to_fp32(output, input);
@@ -162,6 +170,7 @@ static void registry_conversions() {
   // both the vector body and the tail run; checked against the host casts.
   const int n = 1003;
   Tensor src({n}, ScalarType::kFP32, cpu);
+  src.allocate();
   for (int i = 0; i < n; ++i) src.data_ptr<float>()[i] = (i - 500) * 0.0123457f + 1e-4f * (i % 7);
   std::vector<float> host(src.const_data_ptr<float>(), src.const_data_ptr<float>() + n);
   Tensor h16, b16;
@@ -212,6 +221,7 @@ static void registry_attention_matches_direct_call() {
   for (auto &x : hv) x = __float2half(rnd());
   Tensor q({S, H, D}, ScalarType::kFP16, gpu), k({S, Hkv, D}, ScalarType::kFP16, gpu),
       v({S, Hkv, D}, ScalarType::kFP16, gpu), direct({S, H, D}, ScalarType::kFP16, gpu);
+  for (Tensor *t : {&q, &k, &v, &direct}) t->allocate();
   llmx_copy(cpu, gpu, hq.data(), q.data_ptr(), q.nbytes());
   llmx_copy(cpu, gpu, hk.data(), k.data_ptr(), k.nbytes());
   llmx_copy(cpu, gpu, hv.data(), v.data_ptr(), v.nbytes());
@@ -219,6 +229,7 @@ static void registry_attention_matches_direct_call() {
   for (int h = 0; h < H; ++h) hs[h] = std::exp2(-8.f * (h + 1) / H);
   Tensor slopes_cpu(hs.data(), {H}, ScalarType::kFP32, cpu);
   Tensor slopes({H}, ScalarType::kFP32, gpu);
+  slopes.allocate();
   llmx_copy(cpu, gpu, hs.data(), slopes.data_ptr(), slopes.nbytes());
   const float scale = 1.f / std::sqrt(float(D));
   llmx_single_mha_attention(direct, q, k, v, slopes, scale, 100, 0.f);

@@ -166,6 +166,7 @@ def test_long_prefill_every_head_vs_fp32_oracle_on_gpu():
         ref, lref = oracle.attention_ref_chunked(inp.q, inp.k, inp.v, sm_scale=w.sm_scale, alibi=inp.alibi,
                                                  causal=True, heads=hs)
         assert_close(out[:, :, h0:h0 + 8], ref, w.dtype, f"long prefill heads {h0}-{h0 + 7}")
-        torch.testing.assert_close(lse[:, h0:h0 + 8], lref, atol=2e-3, rtol=0)
+        # with ALiBi the lse reaches ~3e4, where one fp32 ulp is ~2e-3: relative part
+        torch.testing.assert_close(lse[:, h0:h0 + 8], lref, atol=2e-3, rtol=1e-6)
         del ref, lref
     llmx_b200.device_status(0)
