@@ -193,22 +193,28 @@ def work_of(w, inp):
 
 
 def cpu_units_sample(w, inp, n_units, seed=0):
-    """A bounded, seeded sample of (b, h) units copied to the host."""
+    """A bounded, seeded sample of the workload copied to the host: (batch,
+    head) units, or for long sequences (> 4096 rows) blocks of 512 query
+    rows of a (batch, head) against the keys they see, so one sample element
+    stays well under a second of CPU work."""
     import random
 
     rng = random.Random(seed)
-    units = []
     valid_b = [b for b in range(w.batch) if inp.q_lens_list[b] > 0 and inp.kv_lens_list[b] > 0]
-    for _ in range(n_units):
-        units.append((rng.choice(valid_b), rng.randrange(w.n_heads)))
     group = w.n_heads // w.n_kv_heads
     data = []
-    for b, h in units:
+    for _ in range(n_units):
+        b, h = rng.choice(valid_b), rng.randrange(w.n_heads)
         ql, kl = inp.q_lens_list[b], inp.kv_lens_list[b]
+        r0, r1 = 0, ql
+        if ql > 4096:
+            r0 = rng.randrange(0, ql - 512 + 1)
+            r1 = r0 + 512
+        k_end = min(kl, r1 + (kl - ql)) if w.causal else kl  # keys the rows can see (bottom-right)
         kvh = h // group
         a = None if inp.alibi is None else inp.alibi[h : h + 1].cpu()
-        data.append((inp.q[b, :ql, h : h + 1].cpu(), inp.k[b, :kl, kvh : kvh + 1].cpu(),
-                     inp.v[b, :kl, kvh : kvh + 1].cpu(), a, ql, kl))
+        data.append((inp.q[b, r0:r1, h : h + 1].cpu(), inp.k[b, :k_end, kvh : kvh + 1].cpu(),
+                     inp.v[b, :k_end, kvh : kvh + 1].cpu(), a, r1 - r0, k_end))
     return data
 
 
@@ -596,7 +602,7 @@ def run_ours(args):
         sample = cpu_units_sample(w, inp, args.cpu_units)
         rate, secs, threads = cpu_oracle_rate(w, sample, repeats=args.cpu_repeats)
         cpu = {"value": rate / (1e9 if w.is_decode else 1e12), "unit": head["unit"], "cores": threads,
-               "kind": "port", "sample": f"{len(sample)} seeded (batch, head) units of {w.name}, x{args.cpu_repeats}, "
+               "kind": "port", "sample": f"{len(sample)} seeded (batch, head) units (512-row blocks past 4096 rows) of {w.name}, x{args.cpu_repeats}, "
                                          f"through the CPU oracle: {secs:.1f} s on {threads} threads"}
     if world > 1:
         import torch.distributed as dist

@@ -92,6 +92,52 @@ __device__ __forceinline__ void stage_rows(float *dst, int dst_pitch, const T *s
   }
 }
 
+// Stages key rows [n0, n0 + kBN) of K (pitch DMAX + 1) and V (pitch DMAX)
+// together: with 16-byte rows every thread issues all of its K and V loads
+// of the tile (up to 16) before storing any, so the tile costs one memory
+// round trip instead of one per load.
+template <typename T, int DMAX>
+__device__ __forceinline__ void stage_kv(float *Ks, float *Vs, const T *kp, const T *vp, long long ks, long long vs,
+                                         int n0, int valid, int D, bool vec) {
+  constexpr int kE = 16 / sizeof(T);
+  constexpr int kUpr = DMAX / kE;                    // 16-byte units per row
+  constexpr int kUnits = kBN * kUpr;                 // per tensor
+  constexpr int kPer = kUnits / kThreads;            // per thread and tensor
+  constexpr int kBatch = kPer < 8 ? kPer : 8;        // loads per tensor in flight
+  static_assert(kUnits % kThreads == 0 && kPer % kBatch == 0, "tile shape");
+  if (!vec) {
+    stage_rows<T, DMAX>(Ks, DMAX + 1, kp, ks, n0, kBN, valid, D, false);
+    stage_rows<T, DMAX>(Vs, DMAX, vp, vs, n0, kBN, valid, D, false);
+    return;
+  }
+#pragma unroll 1
+  for (int b0 = 0; b0 < kPer; b0 += kBatch) {
+    uint4 rk[kBatch], rv[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int idx = threadIdx.x + (b0 + u) * kThreads;
+      const int r = idx / kUpr, x = idx - r * kUpr;
+      rk[u] = rv[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (n0 + r < valid && x * kE < D) {
+        rk[u] = *reinterpret_cast<const uint4 *>(kp + (long long)(n0 + r) * ks + x * kE);
+        rv[u] = *reinterpret_cast<const uint4 *>(vp + (long long)(n0 + r) * vs + x * kE);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int idx = threadIdx.x + (b0 + u) * kThreads;
+      const int r = idx / kUpr, x = idx - r * kUpr;
+      float f[kE];
+      unpack16<T>(rk[u], f);
+#pragma unroll
+      for (int i = 0; i < kE; ++i) Ks[r * (DMAX + 1) + x * kE + i] = f[i];
+      unpack16<T>(rv[u], f);
+#pragma unroll
+      for (int i = 0; i < kE; ++i) Vs[r * DMAX + x * kE + i] = f[i];
+    }
+  }
+}
+
 template <typename T, int DMAX, int kBM>
 __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a, bool vec) {
   using Sm = SimtSmem<DMAX, kBM>;
@@ -149,8 +195,7 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a, bool ve
   __syncthreads();
 
   for (int n0 = lo; n0 < hi; n0 += kBN) {
-    stage_rows<T, DMAX>(Ks, DMAX + 1, kp, a.ks[1], n0, kBN, kl, D, vec);
-    stage_rows<T, DMAX>(Vs, DMAX, vp, a.vs[1], n0, kBN, kl, D, vec);
+    stage_kv<T, DMAX>(Ks, Vs, kp, vp, a.ks[1], a.vs[1], n0, kl, D, vec);
     __syncthreads();
     // Scores: 16 x 64 entries, 8 per thread, lanes along keys.
     for (int e = tid; e < kBM * kBN; e += kThreads) {

@@ -57,6 +57,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity, ui
   return ok != 0;
 }
 
+// Non-blocking: has the phase of `bar` with parity `parity` completed?
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase of `bar` with parity `parity` to complete, for at most
 // `timeout_ns`.  Returns false on timeout (the caller records the error and
 // unwinds); never spins forever.  Waiting threads sleep in try_wait instead
