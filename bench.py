@@ -378,10 +378,12 @@ def bench_kv_split(steps, warmup, rank, world, device, stream, peaks, unsplit):
     """Long-context prefill (B1 H32 S32768 D128 bf16, causal + ALiBi) with its
     keys split over all ranks (parallel.KVSplitPlan.contiguous: one
     work-balanced key range per rank, each rank computing only the rows that
-    can see its keys, row slices exchanged point to point over NCCL, merged
-    by the library's log-sum-exp kernel); strong scaling.  Timed with the
-    output row-sharded (the headline of the leg) and replicated (plus an
-    NCCL all-gather of the slices)."""
+    can see its keys, merged per row slice by the library's log-sum-exp
+    kernel); strong scaling.  Two exchanges are timed: "fused" (the attention
+    kernel writes each row straight into the owning rank's buffer over NVLink
+    through CUDA IPC, then one barrier) -- the leg's headline -- and "nccl"
+    (row slices sent point to point by NCCL after the kernel); each with the
+    output row-sharded and replicated (plus an NCCL all-gather)."""
     from llmx_b200 import parallel
     from llmx_b200.workloads import WORKLOADS, flops, make_inputs
 
@@ -393,32 +395,38 @@ def bench_kv_split(steps, warmup, rank, world, device, stream, peaks, unsplit):
     kc = [inp.k[:, a:b] for a, b in mine]
     vc = [inp.v[:, a:b] for a, b in mine]
     fl = flops(w, [S], [S])
-    res = {"kernel": "tcgen05 (row-restricted partial) + NCCL point-to-point row slices + lse merge kernel",
+    ex = parallel.PeerExchange(plan, 1, w.n_heads, w.head_dim, w.dtype, device)
+    res = {"kernel": "tcgen05 (row-restricted partial) + row-slice exchange + lse merge kernel",
            "plan": {"key_ranges": [list(c) for c in plan.chunks], "first_rows": [plan.first_row(r) for r in range(world)],
                     "slice_rows": plan.slice_rows}}
-    for output in ("sharded", "replicated"):
-        holder = {}
+    for name, exch in (("fused", ex), ("nccl", None)):
+        for output in ("sharded", "replicated"):
+            holder = {}
 
-        def step():
-            marks = []
-            holder["r"] = parallel.kv_split_attention(inp.q, kc, vc, plan, w.sm_scale, alibi_slopes=inp.alibi,
-                                                      output=output, timings=marks)
-            return marks
+            def step():
+                marks = []
+                holder["r"] = parallel.kv_split_attention(inp.q, kc, vc, plan, w.sm_scale, alibi_slopes=inp.alibi,
+                                                          output=output, timings=marks, exchange=exch)
+                return marks
 
-        per, phases = _timed(step, steps, warmup, stream, world)
-        res[output] = {"value": fl / (per * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": per,
-                       "phase_ms_max_over_ranks": phases}
-        if output == "sharded":
-            out, lse, (lo, hi) = holder["r"]
-            res["parity"] = check_parity(out, lse, inp.q, inp.k, inp.v, w, inp.alibi, (lo, hi), range(w.n_heads),
-                                         unsplit[:, lo:hi], world, device)
-        del holder
-    sh = res["sharded"]
-    res.update({"value": sh["value"], "unit": "TFLOP/s", "ms_per_step": sh["ms_per_step"], "scaling": "strong",
-                "output": "row-sharded (each rank holds the merged rows of its slice); 'replicated' adds the all-gather",
-                "roofline": {"bound": "tensor", "achieved": fl / world / (sh["ms_per_step"] * 1e-3) / 1e12,
+            per, phases = _timed(step, steps, warmup, stream, world)
+            key = f"{name}_{output}"
+            res[key] = {"value": fl / (per * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": per,
+                        "phase_ms_max_over_ranks": phases}
+            if output == "sharded":
+                out, lse, (lo, hi) = holder["r"]
+                res[key]["parity"] = check_parity(out, lse, inp.q, inp.k, inp.v, w, inp.alibi, (lo, hi),
+                                                  range(w.n_heads), unsplit[:, lo:hi], world, device)
+            del holder
+    ex.close()
+    head = res["fused_sharded"]
+    res.update({"value": head["value"], "unit": "TFLOP/s", "ms_per_step": head["ms_per_step"], "scaling": "strong",
+                "parity": head["parity"],
+                "output": "row-sharded (each rank holds the merged rows of its slice), fused exchange; the other "
+                          "three lines: replicated output (all-gather) and NCCL point-to-point exchange",
+                "roofline": {"bound": "tensor", "achieved": fl / world / (head["ms_per_step"] * 1e-3) / 1e12,
                              "peak": peaks["bf16_tflops"], "unit": "TFLOP/s per GPU",
-                             "frac": fl / world / (sh["ms_per_step"] * 1e-3) / 1e12 / peaks["bf16_tflops"]}})
+                             "frac": fl / world / (head["ms_per_step"] * 1e-3) / 1e12 / peaks["bf16_tflops"]}})
     return res
 
 

@@ -193,6 +193,49 @@ LLMX_API llmx_status llmx_attn_lse_merge(int32_t n_parts, const llmx_merge_part 
                                          int32_t batch, int32_t seq, int32_t n_heads, int32_t head_dim, void *out,
                                          const int64_t *out_stride, float *lse_out, void *stream);
 
+/* Row-scattered partial output: the tensor-core prefill writes query row R
+ * (global row row_base + local row) of its partial O and lse into
+ * destination p = R / slice_rows, at row R - p * slice_rows of
+ *   o[p]   : [batch, slice_rows, n_heads, head_dim] in the input dtype
+ *   lse[p] : [batch, n_heads, slice_rows] fp32 (natural log)
+ * instead of p->o / p->lse.  The pointers may be another GPU's memory mapped
+ * into this process (llmx_ipc_open): a rank of a KV split then delivers each
+ * row of its partial straight to the rank that merges that row, while the
+ * kernel runs, and every thread fences its writes system-wide before it
+ * exits, so a cross-GPU barrier after the launch (an NCCL all-reduce on the
+ * same stream) orders them before the owner's merge.  No counterpart in the
+ * reference (it has no key splitting).  n_dst <= 8; slice_rows and row_base
+ * multiples of 16; every row the launch computes (row_base .. row_base +
+ * max_q_len - 1) must fall in a destination; pointers 16-byte aligned. */
+#define LLMX_SCATTER_MAX_DST 8
+typedef struct llmx_row_scatter {
+  int32_t n_dst;
+  int32_t slice_rows;
+  int32_t row_base;
+  int32_t reserved;
+  void *o[LLMX_SCATTER_MAX_DST];
+  float *lse[LLMX_SCATTER_MAX_DST];
+} llmx_row_scatter;
+
+/* llmx_attn_fwd with the output rows scattered as *x describes (p->o and
+ * p->lse are ignored).  Runs only on the tensor-core prefill (fp16/bf16,
+ * head_dim 64/128); LLMX_ERR_UNSUPPORTED otherwise. */
+LLMX_API llmx_status llmx_attn_fwd_scatter(const llmx_attn_params *p, const llmx_row_scatter *x, void *stream);
+
+/* Device buffers shared between the GPUs of one node (one process per GPU)
+ * through CUDA IPC, for llmx_attn_fwd_scatter's destinations.  Set-up only,
+ * not for the per-call path: llmx_ipc_alloc allocates `bytes` of device
+ * memory on the current device (zeroed) and writes its 64-byte IPC handle;
+ * another process opens it with llmx_ipc_open (on its own current device, with
+ * peer access enabled as needed) and gets a pointer it can store to;
+ * llmx_ipc_close unmaps an opened pointer; llmx_ipc_free frees a buffer this
+ * process allocated (after every peer has closed it). */
+#define LLMX_IPC_HANDLE_BYTES 64
+LLMX_API llmx_status llmx_ipc_alloc(size_t bytes, void **ptr, void *handle);
+LLMX_API llmx_status llmx_ipc_open(const void *handle, void **ptr);
+LLMX_API llmx_status llmx_ipc_close(void *ptr);
+LLMX_API llmx_status llmx_ipc_free(void *ptr);
+
 /* Element-type conversion of n contiguous elements between fp32, fp16 and
  * bf16 (round to nearest even), enqueued on `stream`.  Replaces the
  * reference's llmx_copy(ScalarType, ScalarType, ...) (src/tensor.cpp:108-118)

@@ -78,6 +78,21 @@ class MergePart(ctypes.Structure):
     ]
 
 
+class RowScatter(ctypes.Structure):
+    """Mirror of ``llmx_row_scatter``."""
+
+    _fields_ = [
+        ("n_dst", _i32),
+        ("slice_rows", _i32),
+        ("row_base", _i32),
+        ("reserved", _i32),
+        ("o", _vp * 8),
+        ("lse", _vp * 8),
+    ]
+
+
+IPC_HANDLE_BYTES = 64
+
 # Every function include/llmx_attn.h declares: name -> (restype, argtypes).
 SIGNATURES = {
     "llmx_attn_params_init": (_i32, [ctypes.POINTER(AttnParams)]),
@@ -95,6 +110,11 @@ SIGNATURES = {
         [_i32, ctypes.POINTER(MergePart), _i32, _i32, _i32, _i32, _i32, _vp, ctypes.POINTER(ctypes.c_int64), _vp,
          _vp],
     ),
+    "llmx_attn_fwd_scatter": (_i32, [ctypes.POINTER(AttnParams), ctypes.POINTER(RowScatter), _vp]),
+    "llmx_ipc_alloc": (_i32, [ctypes.c_size_t, ctypes.POINTER(_vp), _vp]),
+    "llmx_ipc_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "llmx_ipc_close": (_i32, [_vp]),
+    "llmx_ipc_free": (_i32, [_vp]),
     "llmx_convert": (_i32, [_vp, _i32, _vp, _i32, ctypes.c_size_t, _vp]),
     "llmx_attn_device_status": (_i32, [_i32, _i32]),
     "llmx_status_string": (ctypes.c_char_p, [_i32]),

@@ -148,6 +148,11 @@ llmx_status validate(const llmx_attn_params *p, AttnArgs *a) {
   a->kv_total = p->kv_total;
   a->err = nullptr;
   a->num_sms = 148;
+  a->xs_n = a->xs_slice = a->xs_row_base = 0;
+  for (int i = 0; i < LLMX_SCATTER_MAX_DST; ++i) {
+    a->xs_o[i] = nullptr;
+    a->xs_lse[i] = nullptr;
+  }
   return LLMX_OK;
 }
 
@@ -290,6 +295,83 @@ llmx_status llmx_attn_fwd(const llmx_attn_params *p, void *stream) {
     case LLMX_ALGO_TCGEN05: e = launch_sm100(a, p->workspace, p->workspace_bytes, st); break;
   }
   if (e != cudaSuccess) return fail(LLMX_ERR_CUDA, std::string("launch failed: ") + cudaGetErrorString(e));
+  return LLMX_OK;
+}
+
+llmx_status llmx_attn_fwd_scatter(const llmx_attn_params *p, const llmx_row_scatter *x, void *stream) {
+  AttnArgs a;
+  llmx_status s = validate(p, &a);
+  if (s != LLMX_OK) return s;
+  if (x == nullptr) return fail(LLMX_ERR_INVALID_ARGUMENT, "scatter: x is NULL");
+  int algo = 0;
+  s = choose(a, p->algo, &algo);
+  if (s != LLMX_OK) return s;
+  if (algo != LLMX_ALGO_TCGEN05 || a.D == 256)
+    return fail(LLMX_ERR_UNSUPPORTED, "scatter: needs the tensor-core prefill (fp16/bf16, head_dim 64 or 128)");
+  if (x->n_dst < 1 || x->n_dst > LLMX_SCATTER_MAX_DST)
+    return fail(LLMX_ERR_INVALID_ARGUMENT, "scatter: n_dst must be in [1, 8]");
+  if (x->slice_rows < 16 || x->slice_rows % 16 || x->row_base < 0 || x->row_base % 16)
+    return fail(LLMX_ERR_INVALID_ARGUMENT, "scatter: slice_rows and row_base must be multiples of 16");
+  const long long last = (long long)x->row_base + a.Sq - 1;
+  if (last / x->slice_rows >= x->n_dst)
+    return fail(LLMX_ERR_INVALID_ARGUMENT, "scatter: rows past the last destination's slice");
+  for (int d = x->row_base / x->slice_rows; d <= (int)(last / x->slice_rows); ++d)
+    if (!aligned16(x->o[d]) || x->o[d] == nullptr || x->lse[d] == nullptr)
+      return fail(LLMX_ERR_INVALID_ARGUMENT, "scatter: every destination that gets rows needs o (16-byte aligned) and lse");
+  a.xs_n = x->n_dst;
+  a.xs_slice = x->slice_rows;
+  a.xs_row_base = x->row_base;
+  for (int d = 0; d < LLMX_SCATTER_MAX_DST; ++d) {
+    a.xs_o[d] = d < x->n_dst ? x->o[d] : nullptr;
+    a.xs_lse[d] = d < x->n_dst ? x->lse[d] : nullptr;
+  }
+  int dev = 0;
+  const DeviceInfo *info = nullptr;
+  s = current_device(&dev, &info);
+  if (s != LLMX_OK) return s;
+  a.err = info->err;
+  a.num_sms = info->num_sms;
+  const cudaError_t e = launch_sm100(a, p->workspace, p->workspace_bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(LLMX_ERR_CUDA, std::string("launch failed: ") + cudaGetErrorString(e));
+  return LLMX_OK;
+}
+
+llmx_status llmx_ipc_alloc(size_t bytes, void **ptr, void *handle) {
+  if (ptr == nullptr || handle == nullptr || bytes == 0)
+    return fail(LLMX_ERR_INVALID_ARGUMENT, "ipc alloc: ptr, handle and a size are required");
+  static_assert(sizeof(cudaIpcMemHandle_t) == LLMX_IPC_HANDLE_BYTES, "IPC handle size");
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p != nullptr) cudaFree(p);
+    return fail(LLMX_ERR_CUDA, std::string("ipc alloc: ") + cudaGetErrorString(e));
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return LLMX_OK;
+}
+
+llmx_status llmx_ipc_open(const void *handle, void **ptr) {
+  if (ptr == nullptr || handle == nullptr) return fail(LLMX_ERR_INVALID_ARGUMENT, "ipc open: NULL argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(LLMX_ERR_CUDA, std::string("ipc open: ") + cudaGetErrorString(e));
+  return LLMX_OK;
+}
+
+llmx_status llmx_ipc_close(void *ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return fail(LLMX_ERR_CUDA, std::string("ipc close: ") + cudaGetErrorString(e));
+  return LLMX_OK;
+}
+
+llmx_status llmx_ipc_free(void *ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return fail(LLMX_ERR_CUDA, std::string("ipc free: ") + cudaGetErrorString(e));
   return LLMX_OK;
 }
 

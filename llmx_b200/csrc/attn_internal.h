@@ -35,6 +35,10 @@ struct AttnArgs {
   int kv_total;   // full key length for the causal / window diagonal (0: local)
   unsigned int *err;  // device error word (never null)
   int num_sms;
+  // Row-scattered output (llmx_attn_fwd_scatter); xs_n == 0: the usual o / lse.
+  int xs_n, xs_slice, xs_row_base;
+  void *xs_o[LLMX_SCATTER_MAX_DST];
+  float *xs_lse[LLMX_SCATTER_MAX_DST];
 };
 
 // Split-KV decode plan: how many splits of how many keys.

@@ -773,7 +773,23 @@ __device__ bool softmax_tile(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
   // that every store instruction writes 64 contiguous bytes of 8 rows.
   const int gi = threadIdx.x & 3;
   const int qi_group = qi - gi;
-  T *const obase = static_cast<T *>(a.o) + b * a.os[0] + h * a.os[2];
+  // Row `row` of this (batch, head) goes to obase + row * orow.  Scattered
+  // output (a.xs_n > 0): global row R = xs_row_base + row belongs to
+  // destination R / xs_slice, laid out [batch, xs_slice, H, D] there; the
+  // four rows of a lane group share one destination (slice and base are
+  // multiples of 16).
+  T *obase;
+  long long orow;
+  if (a.xs_n > 0) {
+    const int rg = a.xs_row_base + qi_group;
+    const int p = rg / a.xs_slice;
+    orow = (long long)a.H * a.D;
+    obase = static_cast<T *>(a.xs_o[p]) + ((long long)b * a.xs_slice + (rg - p * a.xs_slice) - qi_group) * orow +
+            (long long)h * a.D;
+  } else {
+    orow = a.os[1];
+    obase = static_cast<T *>(a.o) + b * a.os[0] + h * a.os[2];
+  }
 #pragma unroll 1
   for (int ch = 0; ch < D / 32; ++ch) {
     uint32_t o[32];
@@ -796,11 +812,22 @@ __device__ bool softmax_tile(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int row = qi_group + k;
-      if (row < a.Sq) *reinterpret_cast<uint4 *>(obase + (long long)row * a.os[1] + ch * 32 + gi * 8) = u[k];
+      if (row < a.Sq) *reinterpret_cast<uint4 *>(obase + (long long)row * orow + ch * 32 + gi * 8) = u[k];
     }
   }
-  if (a.lse != nullptr && qi < a.Sq)
-    a.lse[((long long)b * a.H + h) * a.Sq + qi] = valid ? (m_used + log2f(l)) * kLn2 : kNegInf;
+  const float lse_v = valid ? (m_used + log2f(l)) * kLn2 : kNegInf;
+  if (a.xs_n > 0) {
+    if (qi < a.Sq) {
+      const int rr = a.xs_row_base + qi;
+      const int p = rr / a.xs_slice;
+      a.xs_lse[p][((long long)b * a.H + h) * a.xs_slice + (rr - p * a.xs_slice)] = lse_v;
+    }
+    // The destinations may be other GPUs' memory: make this thread's writes
+    // visible system-wide before the kernel ends.
+    __threadfence_system();
+  } else if (a.lse != nullptr && qi < a.Sq) {
+    a.lse[((long long)b * a.H + h) * a.Sq + qi] = lse_v;
+  }
   return !aborted;
 }
 

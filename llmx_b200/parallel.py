@@ -243,16 +243,26 @@ class CudaOps:
     def merge(self, parts, out, lse_out):
         """parts: (o [B, n, H, D], lse [B, H, n], row_lo, row_hi) with n =
         row_hi - row_lo, rows counted in `out`'s row axis."""
+        raw = []
+        for o, l, lo, hi in parts:
+            if o.dtype != out.dtype or l.dtype != torch.float32 or o.stride(-1) != 1 or l.stride(-1) != 1:
+                raise RuntimeError("merge parts: O in the output dtype with unit head_dim stride, fp32 lse")
+            raw.append((o.data_ptr(), (o.stride(0), o.stride(1), o.stride(2)), l.data_ptr(), (l.stride(0), l.stride(1)),
+                        lo, hi))
+        self.merge_raw(raw, out, lse_out)
+
+    def merge_raw(self, parts, out, lse_out):
+        """As merge, with each part given as (o address, o element strides
+        (batch, row, head), lse address, lse strides (batch, head), row_lo,
+        row_hi): device memory the caller guarantees is live."""
         B, S, H, D = out.shape
         if out.dtype not in (torch.float16, torch.bfloat16):
             raise RuntimeError("the KV-split merge takes fp16 or bf16 partials")
         arr = (_lib.MergePart * max(1, len(parts)))()
-        for i, (o, l, lo, hi) in enumerate(parts):
-            if o.dtype != out.dtype or l.dtype != torch.float32 or o.stride(-1) != 1 or l.stride(-1) != 1:
-                raise RuntimeError("merge parts: O in the output dtype with unit head_dim stride, fp32 lse")
-            arr[i].o, arr[i].lse = o.data_ptr(), l.data_ptr()
-            arr[i].o_stride[:] = (o.stride(0), o.stride(1), o.stride(2))
-            arr[i].lse_stride[:] = (l.stride(0), l.stride(1))
+        for i, (optr, ost_p, lptr, lst_p, lo, hi) in enumerate(parts):
+            arr[i].o, arr[i].lse = optr, lptr
+            arr[i].o_stride[:] = tuple(int(x) for x in ost_p)
+            arr[i].lse_stride[:] = tuple(int(x) for x in lst_p)
             arr[i].row_lo, arr[i].row_hi = int(lo), int(hi)
         ost = (ctypes.c_int64 * 3)(out.stride(0), out.stride(1), out.stride(2))
         dt = _lib.DTYPE["bf16" if out.dtype == torch.bfloat16 else "fp16"]
@@ -334,6 +344,142 @@ def merge_slice(parts, plan: KVSplitPlan, rank: int, like: torch.Tensor, *, rows
     return out, lse
 
 
+class PeerExchange:
+    """Receive buffers of every rank of `group`, mapped into every rank's
+    process (CUDA IPC through the library's llmx_ipc_* calls), for the fused
+    KV-split exchange: rank s's attention kernel writes each row of its
+    partial straight into the buffer of the rank that owns the row
+    (llmx_attn_fwd_scatter), so no separate transfer step follows the
+    kernel; a one-element all-reduce on the stream then orders every rank's
+    writes before the merges.
+
+    Layout of a rank's buffer set: for each source rank s, O as
+    [B, slice_rows, H, D] (input dtype), then for each s, lse as
+    [B, H, slice_rows] fp32.  Two sets alternate between calls, so a rank's
+    next kernel never overwrites rows a slower rank is still merging (its
+    next kernel starts only after the next barrier, which that rank enters
+    after its merge).  Collective: every rank of the group constructs it with
+    the same arguments; close() it on every rank before destroying the group.
+    """
+
+    def __init__(self, plan: KVSplitPlan, batch: int, n_heads: int, head_dim: int, dtype: torch.dtype,
+                 device, group=None):
+        import torch.distributed as dist
+
+        self.plan, self.B, self.H, self.D, self.dtype = plan, batch, n_heads, head_dim, dtype
+        self.device = torch.device(device)
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if plan.world != self.world:
+            raise ValueError("the plan is for a different number of ranks")
+        es = torch.tensor([], dtype=dtype).element_size()
+        rows = plan.slice_rows
+        self.o_bytes = -(-batch * rows * n_heads * head_dim * es // 256) * 256
+        self.l_bytes = -(-batch * n_heads * rows * 4 // 256) * 256
+        self.set_bytes = self.world * (self.o_bytes + self.l_bytes)
+        lib = _lib.load()
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.llmx_ipc_alloc(2 * self.set_bytes, ctypes.byref(ptr), handle))
+        self._own = ptr.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.base = []
+        self._opened = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self.base.append(self._own)
+                    continue
+                hb = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES).from_buffer_copy(h)
+                pp = ctypes.c_void_p()
+                _lib.check(lib.llmx_ipc_open(hb, ctypes.byref(pp)))
+                self.base.append(pp.value)
+                self._opened.append(pp.value)
+        self.calls = 0
+
+    def o_addr(self, dst: int, src: int, buf: int) -> int:
+        return self.base[dst] + buf * self.set_bytes + src * self.o_bytes
+
+    def lse_addr(self, dst: int, src: int, buf: int) -> int:
+        return self.base[dst] + buf * self.set_bytes + self.world * self.o_bytes + src * self.l_bytes
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (collective)."""
+        import torch.distributed as dist
+
+        if self._own is None:
+            return
+        lib = _lib.load()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                lib.llmx_ipc_close(ctypes.c_void_p(p))
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            lib.llmx_ipc_free(ctypes.c_void_p(self._own))
+        self._own = None
+
+
+def _fused_kv_split(q, k_chunks, v_chunks, plan, sm_scale, rank, group, alibi_slopes, sliding_window, output,
+                    exchange: PeerExchange, timings):
+    """kv_split_attention's fused path: one scattered kernel per rank, a
+    barrier, the merge of this rank's slice from its own buffer."""
+    import torch.distributed as dist
+
+    B, Sq, H, D = q.shape
+    dev = q.device
+    world = plan.world
+    buf = exchange.calls & 1
+    exchange.calls += 1
+    mine = plan.chunks[rank]
+    if mine:
+        (a, b), = mine
+        r0 = plan.chunk_first_row(a)
+        if r0 < Sq:
+            p, keep = ops.build_params(q[:, r0:], q[:, r0:], k_chunks[0], v_chunks[0], sm_scale, sliding_window,
+                                       alibi_slopes=alibi_slopes, causal=plan.causal, kv_offset=a,
+                                       kv_total=plan.kv_len)
+            x = _lib.RowScatter()
+            x.n_dst, x.slice_rows, x.row_base = world, plan.slice_rows, r0
+            for d in range(world):
+                x.o[d] = exchange.o_addr(d, rank, buf)
+                x.lse[d] = exchange.lse_addr(d, rank, buf)
+            lib = _lib.load()
+            ws = torch.empty(256, dtype=torch.uint8, device=dev)
+            p.workspace, p.workspace_bytes = ws.data_ptr(), 256
+            stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+            _lib.check(lib.llmx_attn_fwd_scatter(ctypes.byref(p), ctypes.byref(x), stream))
+    _mark(timings, "attention", dev)
+    # every rank's scattered writes are fenced system-wide by its kernel; the
+    # all-reduce orders them before this rank's merge
+    flag = torch.zeros(1, dtype=torch.float32, device=dev)
+    dist.all_reduce(flag, group=group)
+    _mark(timings, "exchange", dev)
+    lo, hi = plan.row_slice(rank)
+    rows = plan.slice_rows
+    parts = []
+    for s in range(world):
+        r_lo = max(lo, plan.first_row(s))
+        if hi > r_lo:
+            parts.append((exchange.o_addr(rank, s, buf) + (r_lo - lo) * H * D * q.element_size(),
+                          (rows * H * D, H * D, D),
+                          exchange.lse_addr(rank, s, buf) + (r_lo - lo) * 4, (H * rows, rows),
+                          r_lo - lo, hi - lo))
+    n = rows if output == "replicated" else hi - lo
+    out = torch.empty(B, n, H, D, dtype=q.dtype, device=dev)
+    lse = torch.empty(B, H, n, dtype=torch.float32, device=dev)
+    if hi > lo:
+        l_dst = lse if n == hi - lo else torch.empty(B, H, hi - lo, dtype=torch.float32, device=dev)
+        CudaOps().merge_raw(parts, out[:, :hi - lo], l_dst)
+        if l_dst is not lse:
+            lse[:, :, :hi - lo].copy_(l_dst)
+    _mark(timings, "merge", dev)
+    return out, lse, (lo, hi)
+
+
 def kv_split_attention(
     q: torch.Tensor,
     k_chunks: Sequence[torch.Tensor],
@@ -348,6 +494,7 @@ def kv_split_attention(
     output: str = "sharded",
     backend=None,
     timings: Optional[list] = None,
+    exchange: Optional[PeerExchange] = None,
 ):
     """Attention of all of `q` ([B, q_len, H, D]) over the keys of every rank
     of `group`, where this rank holds the key chunks `k_chunks` / `v_chunks`
@@ -360,6 +507,11 @@ def kv_split_attention(
     the plan must have one rank.  `backend` supplies attend / merge (default
     the CUDA kernels); `timings`, if a list, receives (phase, CUDA event)
     marks after the attention, exchange, merge and gather phases.
+
+    exchange: a PeerExchange for this plan and shape selects the fused path
+    (the kernel scatters its rows straight into their owners' buffers over
+    NVLink; plans with one key range per rank whose first visible row is a
+    multiple of 16).  Without it the rows go by NCCL point to point.
     """
     import torch.distributed as dist
 
@@ -375,6 +527,16 @@ def kv_split_attention(
     if Sq != plan.q_len:
         raise ValueError("q's length differs from the plan's")
     dev = q.device
+
+    if exchange is not None and multi:
+        if any(len(c) > 1 for c in plan.chunks) or any(
+                plan.first_row(r) % 16 for r in range(world) if plan.first_row(r) < Sq):
+            raise ValueError("the fused exchange takes one key range per rank starting on a 16-row boundary")
+        out, lse, (lo, hi) = _fused_kv_split(q, k_chunks, v_chunks, plan, sm_scale, rank, group, alibi_slopes,
+                                             sliding_window, output, exchange, timings)
+        if output == "sharded":
+            return out, lse, (lo, hi)
+        return _gather_slices(out, lse, plan, world, group, timings)
 
     # 1. This rank's partial over its keys, rows [row0, Sq).
     part_o, part_l, row0 = local_partial(q, k_chunks, v_chunks, plan, rank, sm_scale, alibi_slopes=alibi_slopes,
@@ -416,7 +578,17 @@ def kv_split_attention(
         return out, lse, (lo, hi)
 
     # 4. All-gather of the slices.
-    rows = plan.slice_rows
+    return _gather_slices(out, lse, plan, world, group, timings, multi)
+
+
+def _gather_slices(out, lse, plan, world, group, timings, multi=True):
+    """All-gather of every rank's slice (each padded to slice_rows) into the
+    whole output on every rank."""
+    import torch.distributed as dist
+
+    B, rows, H, D = out.shape
+    Sq = plan.q_len
+    dev = out.device
     if multi:
         # concatenated along the batch axis (the layout every backend takes)
         go = torch.empty((world * B,) + tuple(out.shape[1:]), dtype=out.dtype, device=dev)

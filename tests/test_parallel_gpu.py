@@ -8,8 +8,13 @@
 * the merge kernel against the oracle's merge (row ranges, strided views,
   rows a part does not cover holding NaN);
 * unit and head shards against the unsplit call (bit-identical);
-* with two or more GPUs, the real 2-rank NCCL split (both plans, both output
-  forms, the short sequences where a rank holds one chunk or none).
+* the row-scattered kernel output (llmx_attn_fwd_scatter) of 2, 4 and 8
+  virtual ranks into per-destination buffers on one GPU, merged per slice,
+  against the unsplit kernel;
+* with two or more GPUs, the real 2-rank split: NCCL point to point (both
+  plans, both output forms, the short sequences where a rank holds one chunk
+  or none) and the fused exchange (the kernel writing into the peer's
+  buffer through CUDA IPC).
 Tolerances: see gpu_helpers.
 """
 import os
@@ -207,3 +212,97 @@ def test_kv_split_two_gpus_nccl(tmp_path, S, make, output):
         lo, hi = res["rows"]
         assert (res["out"].float() - full[:, lo:hi].float().cpu()).abs().max().item() <= 2e-2
         torch.testing.assert_close(res["lse"], lse[:, :, lo:hi].cpu(), atol=1e-3, rtol=0)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_scattered_kernel_output_virtual_ranks(world):
+    import ctypes
+
+    from llmx_b200 import _lib, ops
+
+    S, H, D = 4096, 4, 128
+    q, k, v = (rand(1, S, H, D, seed=s).cuda() for s in range(3))
+    slopes = oracle.alibi_slopes(H).cuda()
+    full = torch.empty_like(q)
+    lfull = torch.empty(1, H, S, device="cuda")
+    llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, alibi_slopes=slopes, lse=lfull)
+    plan = parallel.KVSplitPlan.contiguous(S, world)
+    rows = plan.slice_rows
+    # recv[dst][src]: what source src's kernel writes for destination dst
+    recv_o = [[torch.full((1, rows, H, D), float("nan"), dtype=q.dtype, device="cuda") for _ in range(world)]
+              for _ in range(world)]
+    recv_l = [[torch.full((1, H, rows), float("nan"), device="cuda") for _ in range(world)] for _ in range(world)]
+    lib = _lib.load()
+    for src in range(world):
+        if not plan.chunks[src]:
+            continue
+        (a, b), = plan.chunks[src]
+        r0 = plan.chunk_first_row(a)
+        p, keep = ops.build_params(q[:, r0:], q[:, r0:], k[:, a:b], v[:, a:b], D ** -0.5, alibi_slopes=slopes,
+                                   kv_offset=a, kv_total=S)
+        x = _lib.RowScatter()
+        x.n_dst, x.slice_rows, x.row_base = world, rows, r0
+        for d in range(world):
+            x.o[d] = recv_o[d][src].data_ptr()
+            x.lse[d] = recv_l[d][src].data_ptr()
+        _lib.check(lib.llmx_attn_fwd_scatter(ctypes.byref(p), ctypes.byref(x),
+                                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    out = torch.empty_like(q)
+    for dst in range(world):
+        lo, hi = plan.row_slice(dst)
+        parts = []
+        for src in range(world):
+            r_lo = max(lo, plan.first_row(src))
+            if hi > r_lo:
+                parts.append((recv_o[dst][src][:, r_lo - lo:hi - lo], recv_l[dst][src][:, :, r_lo - lo:hi - lo],
+                              r_lo - lo, hi - lo))
+        o, l = parallel.merge_slice(parts, plan, dst, q)
+        out[:, lo:hi] = o
+        torch.testing.assert_close(l, lfull[:, :, lo:hi], atol=1e-3, rtol=1e-6)
+    torch.cuda.synchronize()
+    assert (out.float() - full.float()).abs().max().item() <= 2e-2
+
+
+def _fused_rank(rank, world, port, S, H, D, path, output):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    q, k, v = (rand(1, S, H, D, seed=s).cuda() for s in range(3))
+    slopes = oracle.alibi_slopes(H).cuda()
+    plan = parallel.KVSplitPlan.contiguous(S, world)
+    ex = parallel.PeerExchange(plan, 1, H, D, q.dtype, q.device)
+    mine = plan.chunks[rank]
+    res = []
+    for _ in range(3):  # both buffer sets, then the first again
+        out, lse, rows = parallel.kv_split_attention(q, [k[:, a:b] for a, b in mine], [v[:, a:b] for a, b in mine],
+                                                     plan, D ** -0.5, alibi_slopes=slopes, output=output, exchange=ex)
+        res.append((out.cpu(), lse.cpu(), rows))
+    torch.cuda.synchronize()
+    ex.close()
+    torch.save(res, f"{path}.{rank}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("output", ["sharded", "replicated"])
+def test_kv_split_two_gpus_fused_exchange(tmp_path, output):
+    S, H, D = 8192, 4, 128
+    path = str(tmp_path / "fused")
+    port = 29700 + (os.getpid() * 7 + len(output)) % 1000
+    mp.spawn(_fused_rank, args=(2, port, S, H, D, path, output), nprocs=2, join=True)
+    q, k, v = (rand(1, S, H, D, seed=s).cuda() for s in range(3))
+    full = torch.empty_like(q)
+    lse = torch.empty(1, H, S, device="cuda")
+    llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, alibi_slopes=oracle.alibi_slopes(H).cuda(),
+                                        lse=lse)
+    torch.cuda.synchronize()
+    for r in range(2):
+        for out, l, (lo, hi) in torch.load(f"{path}.{r}"):
+            assert (out.float() - full[:, lo:hi].float().cpu()).abs().max().item() <= 2e-2
+            torch.testing.assert_close(l, lse[:, :, lo:hi].cpu(), atol=1e-3, rtol=1e-6)
