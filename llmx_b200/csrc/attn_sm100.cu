@@ -98,6 +98,12 @@ struct Cfg {
   static constexpr uint32_t kTmemCols = 512;
 };
 
+// A decoded work item as the TMA thread publishes it in the ring (the
+// consumers copy it instead of each decoding the index again).
+struct ItemPod {
+  int h, b, kvh, ql, kl, m0, n_start, nb, nb0;
+};
+
 struct Bars {
   uint64_t q_full[2], q_empty[2];  // one per query tile
   uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
@@ -107,6 +113,7 @@ struct Bars {
   // index >= n_work) to the MMA thread and the eight softmax warps.
   uint64_t sched_full[kSchedSlots], sched_empty[kSchedSlots];
   int sched_w[kSchedSlots];
+  ItemPod sched_item[kSchedSlots];
   uint32_t tmem_base;
   volatile int abort_flag;
 };
@@ -204,7 +211,10 @@ __device__ __forceinline__ Work decode_work(const AttnArgs &a, int w, int n_mblo
 // each time it finishes issuing the loads of one, so CTAs that drew short
 // items take more of them; without one (one CTA per item) it stops after
 // its first.  Every item index, and a final one >= n_work, goes through the
-// shared-memory ring to the other roles, so all roles see the same sequence.
+// shared-memory ring to the other roles, so all roles see the same sequence;
+// the main kernel's ring slots also carry the decoded item (sched_publish_item
+// / sched_take_item), which saves the MMA thread and the eight softmax warps
+// the integer divisions of decode_work at every item boundary.
 template <typename B>
 __device__ __forceinline__ bool sched_publish(B *bars, int n, int w) {
   const int slot = n % kSchedSlots;
@@ -214,6 +224,32 @@ __device__ __forceinline__ bool sched_publish(B *bars, int n, int w) {
   bars->sched_w[slot] = w;
   mbar_arrive(&bars->sched_full[slot]);  // release: orders the store above
   return true;
+}
+__device__ __forceinline__ bool sched_publish_item(Bars *bars, int n, int w, const Work &t) {
+  const int slot = n % kSchedSlots;
+  if (n >= kSchedSlots &&
+      !mbar_wait_or_abort(&bars->sched_empty[slot], ((n / kSchedSlots) - 1) & 1, kTimeoutNs, &bars->abort_flag))
+    return false;
+  bars->sched_w[slot] = w;
+  ItemPod &it = bars->sched_item[slot];
+  it.h = t.h; it.b = t.b; it.kvh = t.kvh; it.ql = t.ql; it.kl = t.kl; it.m0 = t.m0;
+  it.n_start = t.br.n_start; it.nb = t.br.nb; it.nb0 = t.nb0;
+  mbar_arrive(&bars->sched_full[slot]);  // release: orders the stores above
+  return true;
+}
+// sched_take that also copies the published item (valid when w < n_work).
+__device__ __forceinline__ int sched_take_item(Bars *bars, int n, bool warp_wide, Work &t) {
+  const int slot = n % kSchedSlots;
+  bool ok = mbar_wait_or_abort(&bars->sched_full[slot], (n / kSchedSlots) & 1, kTimeoutNs, &bars->abort_flag);
+  if (warp_wide) ok = __all_sync(0xffffffffu, ok);
+  if (!ok) return -1;
+  const int w = *reinterpret_cast<volatile int *>(&bars->sched_w[slot]);
+  const volatile ItemPod &it = bars->sched_item[slot];
+  t.h = it.h; t.b = it.b; t.kvh = it.kvh; t.ql = it.ql; t.kl = it.kl; t.m0 = it.m0;
+  t.br.n_start = it.n_start; t.br.nb = it.nb; t.nb0 = it.nb0;
+  if (warp_wide) __syncwarp();
+  if (!warp_wide || (threadIdx.x % 32) == 0) mbar_arrive(&bars->sched_empty[slot]);
+  return w;
 }
 
 // The n-th item of the sequence for a consumer role, or -1 on abort.  One
@@ -906,12 +942,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int kv = 0, it = 0;
       int w = (int)blockIdx.x;
       for (int seq = 0;; ++seq) {
-        if (!sched_publish(bars, seq, w)) {
+        Work t{};
+        if (w < n_work) t = decode_work(a, w, n_mblocks, group_units);
+        if (!sched_publish_item(bars, seq, w, t)) {
           set_abort(bars, a.err);
           break;
         }
         if (w >= n_work) break;
-        const Work t = decode_work(a, w, n_mblocks, group_units);
         if (t.br.nb > 0) {
           uint4 beta = make_uint4(0u, 0u, 0u, 0u);
           if constexpr (kFold) {
@@ -937,13 +974,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kMmaWarp && lane == 0) {
       int kv = 0, it = 0, blk0 = 0;
       for (int seq = 0;; ++seq) {
-        const int w = sched_take(bars, seq, false);
+        Work t;
+        const int w = sched_take_item(bars, seq, false, t);
         if (w < 0) {
           set_abort(bars, a.err);
           break;
         }
         if (w >= n_work) break;
-        const Work t = decode_work(a, w, n_mblocks, group_units);
         if (t.br.nb == 0) continue;
         const bool ok = mma_tile<D, std::is_same<T, __nv_bfloat16>::value, kFold, kAlibi>(smem, bars, tmem, t.br.nb,
                                                                                             t.nb0, it, kv, blk0, kv);
@@ -963,13 +1000,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     regs_increase<kRegsSoftmax>();
     int blk = 0;
     for (int seq = 0;; ++seq) {
-      const int w = sched_take(bars, seq, true);
+      Work t;
+      const int w = sched_take_item(bars, seq, true, t);
       if (w < 0) {
         set_abort(bars, a.err);
         break;
       }
       if (w >= n_work) break;
-      const Work t = decode_work(a, w, n_mblocks, group_units);
       if (!softmax_tile<T, D, kAlibi, kSoftcap>(a, bars, tmem, warp, t, blk)) break;
       blk += warp < 4 ? t.nb0 : t.br.nb;
     }
