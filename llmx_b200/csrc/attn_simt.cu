@@ -26,10 +26,16 @@ namespace {
 constexpr int kBN = 64;
 constexpr int kThreads = 128;
 
+// Row pitch of the K tile in shared memory: 16-byte aligned rows, and the
+// 4-word skew spreads the 16-byte reads of lanes on consecutive rows over
+// all 32 banks.
+template <int DMAX>
+constexpr int kKPitch = DMAX + 4;
+
 template <int DMAX, int kBM>
 struct SimtSmem {
   static constexpr int kQ = kBM * DMAX;
-  static constexpr int kK = kBN * (DMAX + 1);
+  static constexpr int kK = kBN * kKPitch<DMAX>;
   static constexpr int kV = kBN * DMAX;
   static constexpr int kS = kBM * kBN;
   static constexpr size_t bytes = sizeof(float) * (kQ + kK + kV + kS + 3 * kBM);
@@ -92,7 +98,7 @@ __device__ __forceinline__ void stage_rows(float *dst, int dst_pitch, const T *s
   }
 }
 
-// Stages key rows [n0, n0 + kBN) of K (pitch DMAX + 1) and V (pitch DMAX)
+// Stages key rows [n0, n0 + kBN) of K (pitch kKPitch) and V (pitch DMAX)
 // together: with 16-byte rows every thread issues all of its K and V loads
 // of the tile (up to 16) before storing any, so the tile costs one memory
 // round trip instead of one per load.
@@ -106,7 +112,7 @@ __device__ __forceinline__ void stage_kv(float *Ks, float *Vs, const T *kp, cons
   constexpr int kBatch = kPer < 8 ? kPer : 8;        // loads per tensor in flight
   static_assert(kUnits % kThreads == 0 && kPer % kBatch == 0, "tile shape");
   if (!vec) {
-    stage_rows<T, DMAX>(Ks, DMAX + 1, kp, ks, n0, kBN, valid, D, false);
+    stage_rows<T, DMAX>(Ks, kKPitch<DMAX>, kp, ks, n0, kBN, valid, D, false);
     stage_rows<T, DMAX>(Vs, DMAX, vp, vs, n0, kBN, valid, D, false);
     return;
   }
@@ -130,13 +136,54 @@ __device__ __forceinline__ void stage_kv(float *Ks, float *Vs, const T *kp, cons
       float f[kE];
       unpack16<T>(rk[u], f);
 #pragma unroll
-      for (int i = 0; i < kE; ++i) Ks[r * (DMAX + 1) + x * kE + i] = f[i];
+      for (int i = 0; i < kE; ++i) Ks[r * kKPitch<DMAX> + x * kE + i] = f[i];
       unpack16<T>(rv[u], f);
 #pragma unroll
       for (int i = 0; i < kE; ++i) Vs[r * DMAX + x * kE + i] = f[i];
     }
   }
 }
+
+// A key tile held in registers between its loads and its shared-memory
+// stores, so the next tile's loads can be in flight while the current tile
+// is computed (layouts with 16-byte rows whose tile is one batch of loads:
+// kPer <= 8 units per thread and tensor).
+template <typename T, int DMAX>
+struct KVPrefetch {
+  static constexpr int kE = 16 / sizeof(T);
+  static constexpr int kUpr = DMAX / kE;
+  static constexpr int kPer = kBN * kUpr / kThreads;
+  static constexpr bool kUsable = kPer <= 8 && kPer * kThreads == kBN * kUpr;
+  uint4 rk[kPer], rv[kPer];
+
+  __device__ __forceinline__ void load(const T *kp, const T *vp, long long ks, long long vs, int n0, int valid,
+                                       int D) {
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int idx = threadIdx.x + u * kThreads;
+      const int r = idx / kUpr, x = idx - r * kUpr;
+      rk[u] = rv[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (n0 + r < valid && x * kE < D) {
+        rk[u] = *reinterpret_cast<const uint4 *>(kp + (long long)(n0 + r) * ks + x * kE);
+        rv[u] = *reinterpret_cast<const uint4 *>(vp + (long long)(n0 + r) * vs + x * kE);
+      }
+    }
+  }
+  __device__ __forceinline__ void store(float *Ks, float *Vs) const {
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int idx = threadIdx.x + u * kThreads;
+      const int r = idx / kUpr, x = idx - r * kUpr;
+      float f[kE];
+      unpack16<T>(rk[u], f);
+#pragma unroll
+      for (int i = 0; i < kE; ++i) Ks[r * kKPitch<DMAX> + x * kE + i] = f[i];
+      unpack16<T>(rv[u], f);
+#pragma unroll
+      for (int i = 0; i < kE; ++i) Vs[r * DMAX + x * kE + i] = f[i];
+    }
+  }
+};
 
 template <typename T, int DMAX, int kBM>
 __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a, bool vec) {
@@ -185,31 +232,65 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a, bool ve
   }
   lo = (lo / kBN) * kBN;
 
-  // Output mapping: thread -> (row r_o, columns d_o + kCols i).
+  // Output mapping: thread -> row r_o, columns 4 d_o + 4 kCols g + (0..3)
+  // for g < kPer / 4 (one 16-byte read of a V row per group and key).
   const int r_o = tid / kCols;
   const int d_o = tid % kCols;
   constexpr int kPer = DMAX / kCols;
+  static_assert(kPer % 4 == 0, "four consecutive output columns per group");
   float acc[kPer];
 #pragma unroll
   for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
   __syncthreads();
 
+  using Pf = KVPrefetch<T, DMAX>;
+  Pf pf;
+  const bool prefetch = Pf::kUsable && vec;
+  if (prefetch && lo < hi) pf.load(kp, vp, a.ks[1], a.vs[1], lo, kl, D);
   for (int n0 = lo; n0 < hi; n0 += kBN) {
-    stage_kv<T, DMAX>(Ks, Vs, kp, vp, a.ks[1], a.vs[1], n0, kl, D, vec);
+    if (prefetch) {
+      pf.store(Ks, Vs);
+      // the next tile's loads fly while this one is computed
+      if (n0 + kBN < hi) pf.load(kp, vp, a.ks[1], a.vs[1], n0 + kBN, kl, D);
+    } else {
+      stage_kv<T, DMAX>(Ks, Vs, kp, vp, a.ks[1], a.vs[1], n0, kl, D, vec);
+    }
     __syncthreads();
-    // Scores: 16 x 64 entries, 8 per thread, lanes along keys.
-    for (int e = tid; e < kBM * kBN; e += kThreads) {
-      const int r = e / kBN, c = e % kBN;
-      const int i = q0 + r, j = n0 + c;
-      float s = -CUDART_INF_F;
-      if (i < ql && key_visible(i, j, kl, doff, a.causal, a.window)) {
-        float dot = 0.f;
-        const float *qr = Qs + r * DMAX;
-        const float *kr = Ks + c * (DMAX + 1);
-        for (int d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
-        s = score_transform(dot, a.sm_scale, a.softcap, slope, j + a.kv_offset);
+    // Scores: kBM x kBN entries; thread t takes key column c = t % kBN of
+    // kSc rows (t / kBN + g * kThreads / kBN), so one 16-byte read of its K
+    // row feeds kSc independent dot products (Q reads are warp broadcasts).
+    // Columns past D are zero in both tiles, so the sums over DMAX equal
+    // the sums over D, accumulated in the same order.
+    {
+      constexpr int kSc = kBM * kBN / kThreads;
+      static_assert(kThreads % kBN == 0, "one key column per thread");
+      const int c = tid % kBN;
+      const int rb = tid / kBN;
+      float dot[kSc];
+#pragma unroll
+      for (int g = 0; g < kSc; ++g) dot[g] = 0.f;
+      const float *kr = Ks + c * kKPitch<DMAX>;
+#pragma unroll 4
+      for (int d = 0; d < DMAX; d += 4) {
+        const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
+#pragma unroll
+        for (int g = 0; g < kSc; ++g) {
+          const float4 q4 = *reinterpret_cast<const float4 *>(Qs + (rb + g * (kThreads / kBN)) * DMAX + d);
+          dot[g] = fmaf(q4.x, k4.x, dot[g]);
+          dot[g] = fmaf(q4.y, k4.y, dot[g]);
+          dot[g] = fmaf(q4.z, k4.z, dot[g]);
+          dot[g] = fmaf(q4.w, k4.w, dot[g]);
+        }
       }
-      Ss[e] = s;
+#pragma unroll
+      for (int g = 0; g < kSc; ++g) {
+        const int r = rb + g * (kThreads / kBN);
+        const int i = q0 + r, j = n0 + c;
+        float s = -CUDART_INF_F;
+        if (i < ql && key_visible(i, j, kl, doff, a.causal, a.window))
+          s = score_transform(dot[g], a.sm_scale, a.softcap, slope, j + a.kv_offset);
+        Ss[r * kBN + c] = s;
+      }
     }
     __syncthreads();
     // Online softmax: warp w owns rows 4w .. 4w+3.
@@ -247,9 +328,15 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a, bool ve
       for (int i = 0; i < kPer; ++i) acc[i] *= alpha;
       for (int c = 0; c < kBN; ++c) {
         const float p = pr[c];
-        const float *vr = Vs + c * DMAX + d_o;
+        const float *vr = Vs + c * DMAX + 4 * d_o;
 #pragma unroll
-        for (int i = 0; i < kPer; ++i) acc[i] = fmaf(p, vr[kCols * i], acc[i]);
+        for (int g = 0; g < kPer / 4; ++g) {
+          const float4 v4 = *reinterpret_cast<const float4 *>(vr + 4 * kCols * g);
+          acc[4 * g] = fmaf(p, v4.x, acc[4 * g]);
+          acc[4 * g + 1] = fmaf(p, v4.y, acc[4 * g + 1]);
+          acc[4 * g + 2] = fmaf(p, v4.z, acc[4 * g + 2]);
+          acc[4 * g + 3] = fmaf(p, v4.w, acc[4 * g + 3]);
+        }
       }
     }
     __syncthreads();
@@ -261,7 +348,7 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a, bool ve
     const float inv = (l > 0.f && qi < ql) ? 1.f / l : 0.f;
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
-      const int d = d_o + kCols * i;
+      const int d = 4 * d_o + 4 * kCols * (i / 4) + (i % 4);
       if (d < D) op[qi * a.os[1] + d] = Elem<T>::from_f(acc[i] * inv);
     }
     if (a.lse != nullptr && d_o == 0) {
