@@ -293,25 +293,39 @@ struct TmaCounts {
 // once the previous item's last QK^T on it has completed (q_empty).
 // With kFold the thread also writes the item's ALiBi row (beta: the slope
 // over sm_scale as three 16-bit parts) into A'_q before signalling Q_q.
-template <int D, bool kFold, bool kReverse>
+// The Q load is issued before A'_q is written (the tile's bytes are added
+// to q_full first, the thread's arrival comes after the A' stores), so the
+// load's latency overlaps the slope read and the stores.
+template <typename T, int D, bool kFold, bool kReverse>
 __device__ bool tma_tile(const CUtensorMap *tm_q, const CUtensorMap *tm_k, const CUtensorMap *tm_v, uint8_t *smem,
-                         Bars *bars, const Work &t, int tile_it, int kv_base, TmaCounts &n, uint4 beta) {
+                         Bars *bars, const Work &t, int tile_it, int kv_base, TmaCounts &n, const AttnArgs &a) {
   using C = Cfg<D>;
   auto wait = [&](uint64_t *bar, uint32_t par) {
     return mbar_wait_or_abort(bar, par, kTimeoutNs, &bars->abort_flag);
   };
+  uint4 beta = make_uint4(0u, 0u, 0u, 0u);
   auto load_q = [&](int q) {
     if (tile_it > 0 && !wait(&bars->q_empty[q], (tile_it - 1) & 1)) return false;
+    mbar_expect_tx(&bars->q_full[q], C::kTileBytes);
+    for (int c = 0; c < C::kChunks; ++c)
+      tma_load_4d(smem + C::kQOff + q * C::kTileBytes + c * C::kChunkBytes, tm_q, &bars->q_full[q], c * 64, t.h,
+                  t.m0 + q * kBM, t.b);
     if constexpr (kFold) {
+      if (q == 0) {
+        // beta = slope / sm_scale as three 16-bit parts (each the rounding
+        // of what the previous ones leave), in columns 0-2.
+        const float b = a.alibi[t.h] / a.sm_scale;
+        const float r1 = b - Elem<T>::to_f(Elem<T>::from_f(b));
+        const float r2 = r1 - Elem<T>::to_f(Elem<T>::from_f(r1));
+        const float f[8] = {b, r1, r2, 0.f, 0.f, 0.f, 0.f, 0.f};
+        beta = pack8<T>(f);
+      }
       uint8_t *xa = smem + C::kXOff + q * C::kXBytes;
 #pragma unroll 8
       for (int r = 0; r < kBM; ++r) *reinterpret_cast<uint4 *>(xa + x_offset(r, 0)) = beta;
       fence_proxy_async_smem();
     }
-    mbar_arrive_expect_tx(&bars->q_full[q], C::kTileBytes);
-    for (int c = 0; c < C::kChunks; ++c)
-      tma_load_4d(smem + C::kQOff + q * C::kTileBytes + c * C::kChunkBytes, tm_q, &bars->q_full[q], c * 64, t.h,
-                  t.m0 + q * kBM, t.b);
+    mbar_arrive(&bars->q_full[q]);
     n.q[q] = tile_it + 1;
     return true;
   };
@@ -851,6 +865,17 @@ __device__ bool softmax_tile(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
       if (row < a.Sq) *reinterpret_cast<uint4 *>(obase + (long long)row * orow + ch * 32 + gi * 8) = u[k];
     }
   }
+  // The unit's last item also writes the rows past the query length that no
+  // item covers (items starting past it are skipped): zeros, lse -inf.
+  if (a.xs_n == 0 && m0 + kTiles * kBM >= ql && m0 + kTiles * kBM < a.Sq) {
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    T *const zbase = static_cast<T *>(a.o) + b * a.os[0] + h * a.os[2];
+    for (int row = m0 + kTiles * kBM + t * kBM + r; row < a.Sq; row += kTiles * kBM) {
+#pragma unroll 4
+      for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4 *>(zbase + (long long)row * a.os[1] + c) = z;
+      if (a.lse != nullptr) a.lse[((long long)b * a.H + h) * a.Sq + row] = kNegInf;
+    }
+  }
   const float lse_v = valid ? (m_used + log2f(l)) * kLn2 : kNegInf;
   if (a.xs_n > 0) {
     if (qi < a.Sq) {
@@ -941,26 +966,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       TmaCounts n;
       int kv = 0, it = 0;
       int w = (int)blockIdx.x;
-      for (int seq = 0;; ++seq) {
+      for (int seq = 0;;) {
         Work t{};
-        if (w < n_work) t = decode_work(a, w, n_mblocks, group_units);
-        if (!sched_publish_item(bars, seq, w, t)) {
+        if (w < n_work) {
+          t = decode_work(a, w, n_mblocks, group_units);
+          // Rows past the sequence's query length: nothing to compute, and the
+          // unit's last item zero-fills them (softmax_tile), so the item is
+          // not published at all.
+          if (t.m0 >= t.ql && t.m0 > 0) {
+            w = work_ctr != nullptr ? (int)gridDim.x + atomicAdd(work_ctr, 1) : n_work;
+            continue;
+          }
+        }
+        if (!sched_publish_item(bars, seq++, w, t)) {
           set_abort(bars, a.err);
           break;
         }
         if (w >= n_work) break;
         if (t.br.nb > 0) {
-          uint4 beta = make_uint4(0u, 0u, 0u, 0u);
-          if constexpr (kFold) {
-            // beta = slope / sm_scale as three 16-bit parts (each the rounding
-            // of what the previous ones leave), in columns 0-2.
-            const float b = a.alibi[t.h] / a.sm_scale;
-            const float r1 = b - Elem<T>::to_f(Elem<T>::from_f(b));
-            const float r2 = r1 - Elem<T>::to_f(Elem<T>::from_f(r1));
-            const float f[8] = {b, r1, r2, 0.f, 0.f, 0.f, 0.f, 0.f};
-            beta = pack8<T>(f);
-          }
-          const bool ok = tma_tile<D, kFold, kAlibi>(&tm_q, &tm_k, &tm_v, smem, bars, t, it, kv, n, beta);
+          const bool ok = tma_tile<T, D, kFold, kAlibi>(&tm_q, &tm_k, &tm_v, smem, bars, t, it, kv, n, a);
           kv += t.br.nb;
           ++it;
           if (!ok) {

@@ -43,6 +43,13 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                : "memory");
 }
 
+// Adds `bytes` to the transaction count of the current phase without an
+// arrival: the phase then needs both these bytes and the expected arrivals.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
 // One bounded sleep on the phase: the thread is suspended until the phase
 // with parity `parity` completes or `hint_ns` passes, whichever is first.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
