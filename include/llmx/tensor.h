@@ -70,6 +70,22 @@ void llmx_free(void *data);
 void llmx_free(void *data, Device device);
 // The record of a block llmx_allocate returned, or nullopt (tensor.cpp:148-153).
 std::optional<MemInfo> llmx_mem_info(void *data);
+
+// Stream-ordered pooling of CUDA storage (off by default; also switched on by
+// the environment variable LLMX_TENSOR_POOL=1 at the first CUDA allocation).
+// When on, llmx_allocate takes CUDA blocks from the device's memory pool
+// with cudaMallocAsync on the legacy default stream (zero-filled there) and
+// llmx_free returns them with cudaFreeAsync on the same stream, keeping the
+// pool's memory cached, so repeated tensor allocation costs no cudaMalloc /
+// cudaFree and no device-wide synchronisation.  The reference runs all of
+// its work on the legacy stream (attention_api.cpp:55), which orders these
+// frees after it.  A caller that uses a tensor on a non-blocking stream must
+// synchronise that stream before the tensor's storage is freed, or the pool
+// may hand the block to another tensor while the work still runs; with the
+// pool off, cudaFree's implicit synchronisation covers that case.  Blocks
+// keep the mode they were allocated in.
+void llmx_set_cuda_pool(bool enabled);
+bool llmx_cuda_pool_enabled();
 void llmx_copy(Device src_device, Device dst_device, const void *src, void *dst, size_t nbytes);
 // Element-type conversion of `num` contiguous elements in device-addressable
 // memory (src/tensor.cpp:108-118), on the legacy stream like the reference's

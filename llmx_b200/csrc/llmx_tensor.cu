@@ -4,6 +4,8 @@
 // to_device moves (optionally copies) storage between host and a CUDA device.
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <cstdint>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -20,16 +22,56 @@ void cuda_ok(cudaError_t e, const char *what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-// Blocks llmx_allocate returned, for llmx_free(void *) and llmx_mem_info.
+// Blocks llmx_allocate returned, for llmx_free(void *) and llmx_mem_info,
+// and which of them came from the stream-ordered pool.
 std::mutex g_blocks_mu;
 std::unordered_map<void *, MemInfo> &blocks() {
   static auto *m = new std::unordered_map<void *, MemInfo>();  // outlives static destructors
   return *m;
 }
+std::unordered_map<void *, bool> &pooled() {
+  static auto *m = new std::unordered_map<void *, bool>();
+  return *m;
+}
 
-void release(void *data, Device device) {
+// -1: not decided yet (read LLMX_TENSOR_POOL at the first CUDA allocation).
+std::atomic<int> g_pool_mode{-1};
+
+bool pool_on() {
+  int m = g_pool_mode.load();
+  if (m < 0) {
+    const char *env = std::getenv("LLMX_TENSOR_POOL");
+    int want = (env != nullptr && env[0] == '1') ? 1 : 0;
+    g_pool_mode.compare_exchange_strong(m, want);
+    m = g_pool_mode.load();
+  }
+  return m == 1;
+}
+
+// Keeps the freed memory of the current device's default pool cached (the
+// pool would otherwise return it to the driver at the next synchronisation).
+void retain_pool_memory(int dev) {
+  static std::once_flag once[64];
+  if (dev < 0 || dev >= 64) return;
+  std::call_once(once[dev], [dev] {
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+      uint64_t keep = UINT64_MAX;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+  });
+}
+
+void release(void *data, Device device, bool from_pool) {
   if (device.type == DeviceType::kCPU) {
     std::free(data);
+  } else if (from_pool) {
+    // Freed on the legacy stream of the device whose pool holds the block.
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device.id < 0 ? 0 : device.id);
+    cudaFreeAsync(data, 0);
+    cudaSetDevice(prev);
   } else {
     cudaFree(data);
   }
@@ -54,41 +96,63 @@ void *llmx_allocate(size_t nbytes, Device device) {
   } else {
     int prev = 0;
     cuda_ok(cudaGetDevice(&prev), "cudaGetDevice");
-    cuda_ok(cudaSetDevice(device.id < 0 ? 0 : device.id), "cudaSetDevice");
-    cudaError_t e = cudaMalloc(&p, nbytes);
-    if (e == cudaSuccess) e = cudaMemset(p, 0, nbytes);
+    const int dev = device.id < 0 ? 0 : device.id;
+    cuda_ok(cudaSetDevice(dev), "cudaSetDevice");
+    const bool from_pool = pool_on();
+    cudaError_t e;
+    if (from_pool) {
+      retain_pool_memory(dev);
+      e = cudaMallocAsync(&p, nbytes, 0);
+      if (e == cudaSuccess) e = cudaMemsetAsync(p, 0, nbytes, 0);
+    } else {
+      e = cudaMalloc(&p, nbytes);
+      if (e == cudaSuccess) e = cudaMemset(p, 0, nbytes);
+    }
     cudaSetDevice(prev);
     if (e != cudaSuccess && p != nullptr) {
-      cudaFree(p);
+      if (from_pool)
+        cudaFreeAsync(p, 0);
+      else
+        cudaFree(p);
       p = nullptr;
     }
-    cuda_ok(e, "cudaMalloc");
+    cuda_ok(e, from_pool ? "cudaMallocAsync" : "cudaMalloc");
+    std::lock_guard<std::mutex> lock(g_blocks_mu);
+    if (from_pool) pooled()[p] = true;
   }
   std::lock_guard<std::mutex> lock(g_blocks_mu);
   blocks()[p] = MemInfo{p, nbytes, device};
   return p;
 }
 
+void llmx_set_cuda_pool(bool enabled) { g_pool_mode.store(enabled ? 1 : 0); }
+
+bool llmx_cuda_pool_enabled() { return pool_on(); }
+
 void llmx_free(void *data) {
   if (data == nullptr) return;
   Device device;
+  bool from_pool = false;
   {
     std::lock_guard<std::mutex> lock(g_blocks_mu);
     auto it = blocks().find(data);
     if (it == blocks().end()) return;
     device = it->second.device;
     blocks().erase(it);
+    from_pool = pooled().erase(data) > 0;
   }
-  release(data, device);
+  release(data, device, from_pool);
 }
 
 void llmx_free(void *data, Device device) {
   if (data == nullptr) return;
+  bool from_pool = false;
   {
     std::lock_guard<std::mutex> lock(g_blocks_mu);
     blocks().erase(data);
+    from_pool = pooled().erase(data) > 0;
   }
-  release(data, device);
+  release(data, device, from_pool);
 }
 
 std::optional<MemInfo> llmx_mem_info(void *data) {

@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <stdexcept>
@@ -261,8 +262,64 @@ static void registry_attention_matches_direct_call() {
   EXPECT(threw);
 }
 
+// The stream-ordered pool: blocks are zero-filled, tracked by llmx_mem_info
+// and reused after a free (the pool's reserved memory does not grow for a
+// second request of the same size), and every block is freed the way it was
+// allocated, whatever the switch says at the time of the free.
+static size_t pool_reserved() {
+  cudaMemPool_t pool;
+  uint64_t bytes = 0;
+  if (cudaDeviceGetDefaultMemPool(&pool, 0) != cudaSuccess) return 0;
+  cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &bytes);
+  return (size_t)bytes;
+}
+
+static bool all_zero_fp16(const Tensor &t) {
+  std::vector<uint16_t> h((size_t)t.numel(), 0xFFFF);
+  llmx_copy(Device(DeviceType::kCUDA, 0), Device(DeviceType::kCPU), t.const_data_ptr(), h.data(), h.size() * 2);
+  for (uint16_t x : h)
+    if (x != 0) return false;
+  return true;
+}
+
+static void pooled_storage() {
+  Device gpu(DeviceType::kCUDA, 0), cpu(DeviceType::kCPU);
+  EXPECT(!llmx_cuda_pool_enabled());
+  Tensor direct({1024}, ScalarType::kFP32, gpu);
+  direct.allocate();
+  llmx_set_cuda_pool(true);
+  EXPECT(llmx_cuda_pool_enabled());
+  void *first = nullptr;
+  size_t reserved = 0;
+  {
+    Tensor t({1 << 20}, ScalarType::kFP16, gpu);
+    t.allocate();
+    first = t.data_ptr();
+    EXPECT(llmx_mem_info(first).has_value() && llmx_mem_info(first)->nbytes == (2u << 20));
+    EXPECT(all_zero_fp16(t));
+    std::vector<uint16_t> ones((size_t)t.numel(), 0x3C00);  // 1.0 in fp16
+    llmx_copy(cpu, gpu, ones.data(), t.data_ptr(), ones.size() * 2);
+    reserved = pool_reserved();
+    EXPECT(reserved >= (2u << 20));
+  }
+  EXPECT(!llmx_mem_info(first).has_value());
+  Tensor again({1 << 20}, ScalarType::kFP16, gpu);
+  again.allocate();
+  EXPECT(pool_reserved() == reserved);  // served from the freed block
+  EXPECT(all_zero_fp16(again));         // re-zeroed, not the previous tensor's ones
+  void *d = direct.data_ptr();
+  direct = Tensor();  // allocated with cudaMalloc: released with cudaFree
+  EXPECT(!llmx_mem_info(d).has_value());
+  llmx_set_cuda_pool(false);
+  void *a = again.data_ptr();
+  again = Tensor();  // allocated from the pool: returned to it
+  EXPECT(!llmx_mem_info(a).has_value());
+  EXPECT(cudaDeviceSynchronize() == cudaSuccess);
+}
+
 int main() {
   tensor_semantics();
+  pooled_storage();
   smoke_zero_inputs();
   known_answer_uniform_weights();
   argument_errors_throw();
