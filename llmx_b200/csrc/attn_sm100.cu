@@ -905,7 +905,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzled tiles want 1024-byte aligned shared-memory addresses.
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Offsetting smem_raw (rather than rounding a cast integer) keeps every
+  // derived pointer known to be in shared memory, so barrier and flag
+  // addresses stay 32-bit shared-window values instead of generic pointers
+  // the compiler would spill.
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Bars *bars = reinterpret_cast<Bars *>(smem + C::kBarOff);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -1345,7 +1349,7 @@ __global__ void __launch_bounds__(kThreads256, 1)
                            const int group_units, const int n_work, int *work_ctr) {
   using C = Cfg256;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Bars256 *bars = reinterpret_cast<Bars256 *>(smem + C::kBarOff);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   constexpr bool kFold = kAlibi && !kSoftcap;

@@ -93,7 +93,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
 
 // As mbar_wait, but also gives up once *abort is non-zero (checked between
 // sleeps): after one role records a timeout, the others stop within one
-// sleep interval instead of each waiting out its own limit.
+// sleep interval instead of each waiting out its own limit.  `abort` is a
+// flag in this CTA's shared memory, read through the shared window (a
+// 32-bit address, so no generic pointer stays live across the caller's loop).
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parity, uint64_t timeout_ns,
                                                    const volatile int *abort) {
   constexpr uint32_t kSleepNs = 100000;
@@ -101,7 +103,9 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parit
   const uint64_t t0 = global_timer_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity, kSleepNs)) return true;
-    if (*abort) return false;
+    uint32_t flag;
+    asm volatile("ld.volatile.shared.b32 %0, [%1];" : "=r"(flag) : "r"(smem_u32((const void *)abort)) : "memory");
+    if (flag != 0) return false;
     if (global_timer_ns() - t0 > timeout_ns) return false;
   }
 }
