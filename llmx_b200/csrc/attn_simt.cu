@@ -212,14 +212,6 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a, bool ve
   T *op = static_cast<T *>(a.o) + b * a.os[0] + h * a.os[2];
   const float slope = a.alibi ? a.alibi[h] : 0.f;
 
-  // Q tile -> fp32 smem (rows past q_len and columns past D are zero).
-  stage_rows<T, DMAX>(Qs, DMAX, qp, a.qs[1], q0, kBM, ql, D, vec);
-  if (tid < kBM) {
-    m_s[tid] = -CUDART_INF_F;
-    l_s[tid] = 0.f;
-    alpha_s[tid] = 1.f;
-  }
-
   // Key range that any row of this tile can see.
   const int doff = diag_shift(a, ql, kl);
   const int r_last = min(q0 + kBM, ql) - 1;
@@ -232,6 +224,21 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a, bool ve
   }
   lo = (lo / kBN) * kBN;
 
+  // The first key tile's loads are issued before the Q tile is staged, so
+  // the two memory round trips overlap.
+  using Pf = KVPrefetch<T, DMAX>;
+  Pf pf;
+  const bool prefetch = Pf::kUsable && vec;
+  if (prefetch && lo < hi) pf.load(kp, vp, a.ks[1], a.vs[1], lo, kl, D);
+
+  // Q tile -> fp32 smem (rows past q_len and columns past D are zero).
+  stage_rows<T, DMAX>(Qs, DMAX, qp, a.qs[1], q0, kBM, ql, D, vec);
+  if (tid < kBM) {
+    m_s[tid] = -CUDART_INF_F;
+    l_s[tid] = 0.f;
+    alpha_s[tid] = 1.f;
+  }
+
   // Output mapping: thread -> row r_o, columns 4 d_o + 4 kCols g + (0..3)
   // for g < kPer / 4 (one 16-byte read of a V row per group and key).
   const int r_o = tid / kCols;
@@ -243,10 +250,6 @@ __global__ void __launch_bounds__(kThreads) attn_simt_kernel(AttnArgs a, bool ve
   for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
   __syncthreads();
 
-  using Pf = KVPrefetch<T, DMAX>;
-  Pf pf;
-  const bool prefetch = Pf::kUsable && vec;
-  if (prefetch && lo < hi) pf.load(kp, vp, a.ks[1], a.vs[1], lo, kl, D);
   for (int n0 = lo; n0 < hi; n0 += kBN) {
     if (prefetch) {
       pf.store(Ks, Vs);

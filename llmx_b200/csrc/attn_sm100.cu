@@ -883,9 +883,6 @@ __device__ bool softmax_tile(const AttnArgs &a, Bars *bars, uint32_t tmem, int w
       const int p = rr / a.xs_slice;
       a.xs_lse[p][((long long)b * a.H + h) * a.xs_slice + (rr - p * a.xs_slice)] = lse_v;
     }
-    // The destinations may be other GPUs' memory: make this thread's writes
-    // visible system-wide before the kernel ends.
-    __threadfence_system();
   } else if (a.lse != nullptr && qi < a.Sq) {
     a.lse[((long long)b * a.H + h) * a.Sq + qi] = lse_v;
   }
@@ -1038,6 +1035,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!softmax_tile<T, D, kAlibi, kSoftcap>(a, bars, tmem, warp, t, blk)) break;
       blk += warp < 4 ? t.nb0 : t.br.nb;
     }
+    // Scattered output may be other GPUs' memory: make this thread's writes
+    // visible system-wide once, after its last item, before the kernel ends.
+    if (a.xs_n > 0) __threadfence_system();
   }
 
   tc_fence_before();

@@ -166,6 +166,93 @@ def causal_key_range(seq_len: int, world: int, rank: int, align: int = 16) -> Tu
     return bound(rank), bound(rank + 1)
 
 
+# Work-item geometry of the tensor-core prefill kernel: items of 256 query
+# rows (two 128-row tiles) over key blocks of 128, and the measured cost of
+# one item's start and epilogue in key-block units (the per-item overhead of
+# the persistent kernel on B200, from timing each rank's partial of a
+# 32768-token causal split).
+ITEM_ROWS = 256
+KEY_BLOCK = 128
+ITEM_COST = 1.5
+
+
+def key_range_cost(a: int, b: int, q_len: int, kv_len: int, *, item_rows: int = ITEM_ROWS,
+                   block: int = KEY_BLOCK, item_cost: float = ITEM_COST) -> float:
+    """Modelled kernel time, in key-block units per head, of the causal
+    partial of keys [a, b) (bottom-right aligned): its rows are those from
+    the first that sees key a; each item of `item_rows` rows costs
+    `item_cost` plus one unit per key block its last row sees."""
+    if b <= a:
+        return 0.0
+    shift = kv_len - q_len
+    r0 = max(0, min(q_len, a - shift))
+    n_items = -(-(q_len - r0) // item_rows)
+    total = 0.0
+    for i in range(n_items):
+        last = min(q_len - 1, r0 + (i + 1) * item_rows - 1)
+        seen = min(b, last + shift + 1) - a
+        if seen > 0:
+            total += item_cost + -(-seen // block)
+    return total
+
+
+def balanced_key_ranges(seq_len: int, world: int, *, align: int = KEY_BLOCK,
+                        item_cost: float = ITEM_COST) -> List[Tuple[int, int]]:
+    """One contiguous key range per rank for a causal self-attention split,
+    chosen to minimise the largest ``key_range_cost`` over the ranks (the
+    kernel-time balance: a rank holding late keys computes a causal
+    triangle of short items, one holding early keys long rectangles).
+
+    Boundaries are multiples of `align` (the last range ends at seq_len);
+    every rank gets at least one block when seq_len >= world * align, else
+    the trailing ranks get empty ranges.  The ranges cover every key once.
+    """
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    n_blk = -(-seq_len // align)
+    eff = max(1, min(world, n_blk))
+    pos = [min(seq_len, i * align) for i in range(n_blk + 1)]
+    cost = lambda i, j: key_range_cost(pos[i], pos[j], seq_len, seq_len, item_cost=item_cost)
+
+    def cut(limit: float) -> Optional[List[int]]:
+        # greedy: each range takes as many blocks as fit under `limit`,
+        # leaving at least one block for every later rank
+        edges = [0]
+        for r in range(eff - 1):
+            i = edges[-1]
+            lo, hi = i + 1, n_blk - (eff - 1 - r)
+            if lo > hi or cost(i, lo) > limit:
+                return None
+            while lo < hi:  # largest j in [lo, hi] with cost(i, j) <= limit
+                mid = (lo + hi + 1) // 2
+                if cost(i, mid) <= limit:
+                    lo = mid
+                else:
+                    hi = mid - 1
+            edges.append(lo)
+        if cost(edges[-1], n_blk) > limit:
+            return None
+        return edges + [n_blk]
+
+    lo_t, hi_t = 0.0, cost(0, n_blk)
+    best = cut(hi_t) if eff == 1 else None
+    for _ in range(60):
+        if eff == 1:
+            break
+        mid = (lo_t + hi_t) / 2
+        e = cut(mid)
+        if e is None:
+            lo_t = mid
+        else:
+            hi_t, best = mid, e
+        if hi_t - lo_t < 1e-3:
+            break
+    if best is None:
+        best = cut(hi_t)
+    ranges = [(pos[best[r]], pos[best[r + 1]]) for r in range(eff)]
+    return ranges + [(seq_len, seq_len)] * (world - eff)
+
+
 def kv_split_ranges(seq_len: int, world: int, rank: int) -> List[Tuple[int, int]]:
     """The key ranges of `rank` for a causal KV split over `world` ranks: one
     contiguous, work-balanced range (``causal_key_range``), or none for a
@@ -191,10 +278,19 @@ class KVSplitPlan:
     causal: bool = True
 
     @classmethod
-    def contiguous(cls, seq_len: int, world: int, causal: bool = True) -> "KVSplitPlan":
-        """One work-balanced key range per rank (``kv_split_ranges``)."""
-        ch = tuple(tuple(kv_split_ranges(seq_len, world, r)) if causal else tuple(_even_range(seq_len, world, r))
-                   for r in range(world))
+    def contiguous(cls, seq_len: int, world: int, causal: bool = True, balance: str = "kernel") -> "KVSplitPlan":
+        """One key range per rank: balanced on the kernel's modelled time
+        (``balanced_key_ranges``, the default) or on visible causal pairs
+        (``balance="pairs"``, ``kv_split_ranges``); even ranges without the
+        causal mask."""
+        if not causal:
+            ch = tuple(tuple(_even_range(seq_len, world, r)) for r in range(world))
+        elif balance == "kernel":
+            ch = tuple(((a, b),) if b > a else () for a, b in balanced_key_ranges(seq_len, world))
+        elif balance == "pairs":
+            ch = tuple(tuple(kv_split_ranges(seq_len, world, r)) for r in range(world))
+        else:
+            raise ValueError("balance must be 'kernel' or 'pairs'")
         return cls(seq_len, seq_len, world, ch, causal)
 
     @classmethod

@@ -75,6 +75,59 @@ def test_causal_key_range_gives_every_rank_a_block_when_possible(S, world):
         assert sum(1 for a, b in ranges if b > a) == -(-S // 16)
 
 
+def _model_cost_bruteforce(a, b, S, item_rows=256, block=128, item_cost=1.5):
+    # item by item, row by row: the item's block count is that of its last row
+    total, r = 0.0, a
+    while r < S:
+        last = min(S - 1, r + item_rows - 1)
+        seen = min(b, last + 1) - a
+        if seen > 0:
+            total += item_cost + -(-seen // block)
+        r += item_rows
+    return total
+
+
+@pytest.mark.parametrize("a,b,S", [(0, 32768, 32768), (0, 100, 1000), (128, 1000, 1000), (384, 1024, 4096),
+                                   (16384, 32768, 32768), (5, 5, 64)])
+def test_key_range_cost_matches_item_by_item_count(a, b, S):
+    assert parallel.key_range_cost(a, b, S, S) == _model_cost_bruteforce(a, b, S)
+
+
+@pytest.mark.parametrize("S,world", [(32768, 2), (32768, 4), (32768, 8), (131072, 8), (1000, 3), (4096, 8),
+                                     (300, 3), (100, 8), (20, 2), (128, 4)])
+def test_balanced_key_ranges_cover_once_aligned_and_balanced(S, world):
+    ranges = parallel.balanced_key_ranges(S, world)
+    assert len(ranges) == world
+    covered = sorted(j for a, b in ranges for j in range(a, b))
+    assert covered == list(range(S))
+    nonempty = [(a, b) for a, b in ranges if b > a]
+    for a, b in nonempty:
+        assert a % 128 == 0 and (b % 128 == 0 or b == S)
+    assert len(nonempty) == min(world, -(-S // 128))
+    assert ranges[:len(nonempty)] == nonempty  # empty ranges only at the end
+    if S >= 32768:
+        cost = [parallel.key_range_cost(a, b, S, S) for a, b in ranges]
+        pairs = [parallel.causal_key_range(S, world, r) for r in range(world)]
+        pair_cost = [parallel.key_range_cost(a, b, S, S) for a, b in pairs]
+        # no worse than the pair-balanced split on the kernel model, and
+        # within a few blocks per rank of the mean
+        assert max(cost) <= max(pair_cost) + 1e-9
+        assert max(cost) - sum(cost) / world < 0.03 * sum(cost) / world
+
+
+def test_contiguous_plan_balance_choice():
+    S, world = 32768, 8
+    kern = parallel.KVSplitPlan.contiguous(S, world)
+    pairs = parallel.KVSplitPlan.contiguous(S, world, balance="pairs")
+    assert [c[0] for c in kern.chunks] == parallel.balanced_key_ranges(S, world)
+    assert [c[0] for c in pairs.chunks] == [parallel.causal_key_range(S, world, r) for r in range(world)]
+    with pytest.raises(ValueError):
+        parallel.KVSplitPlan.contiguous(S, world, balance="rows")
+    # without the causal mask both give even ranges
+    assert parallel.KVSplitPlan.contiguous(S, world, causal=False).chunks == \
+        parallel.KVSplitPlan.contiguous(S, world, causal=False, balance="pairs").chunks
+
+
 @pytest.mark.parametrize("start,end,heads", [(0, 256, 32), (32, 64, 32), (5, 70, 32), (3, 9, 4), (0, 1, 1),
                                              (10, 10, 4)])
 def test_unit_runs_cover_the_range(start, end, heads):

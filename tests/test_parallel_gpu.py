@@ -306,3 +306,29 @@ def test_kv_split_two_gpus_fused_exchange(tmp_path, output):
         for out, l, (lo, hi) in torch.load(f"{path}.{r}"):
             assert (out.float() - full[:, lo:hi].float().cpu()).abs().max().item() <= 2e-2
             torch.testing.assert_close(l, lse[:, :, lo:hi].cpu(), atol=1e-3, rtol=1e-6)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
+@pytest.mark.parametrize("exchange,make,output", [("nccl", "zigzag", "sharded"), ("nccl", "contiguous", "replicated"),
+                                                  ("fused", None, "sharded"), ("fused", None, "replicated")])
+def test_kv_split_four_gpus(tmp_path, exchange, make, output):
+    """Four ranks: every rank's rows against the whole call (O and lse)."""
+    S, H, D, world = 8192, 4, 128, 4
+    path = str(tmp_path / "split4")
+    port = 29800 + (os.getpid() * 7 + len(exchange) + len(output)) % 1000
+    if exchange == "fused":
+        mp.spawn(_fused_rank, args=(world, port, S, H, D, path, output), nprocs=world, join=True)
+    else:
+        mp.spawn(_nccl_rank, args=(world, port, S, H, D, path, make, output), nprocs=world, join=True)
+    q, k, v = (rand(1, S, H, D, seed=s).cuda() for s in range(3))
+    full = torch.empty_like(q)
+    lse = torch.empty(1, H, S, device="cuda")
+    llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, alibi_slopes=oracle.alibi_slopes(H).cuda(),
+                                        lse=lse)
+    torch.cuda.synchronize()
+    for r in range(world):
+        res = torch.load(f"{path}.{r}")
+        runs = res if exchange == "fused" else [(res["out"], res["lse"], res["rows"])]
+        for out, l, (lo, hi) in runs:
+            assert (out.float() - full[:, lo:hi].float().cpu()).abs().max().item() <= 2e-2
+            torch.testing.assert_close(l, lse[:, :, lo:hi].cpu(), atol=1e-3, rtol=1e-6)
