@@ -21,9 +21,18 @@ from . import ops
 
 class HostAttention:
     """Device buffers, streams and events for repeated host-to-host attention
-    calls of one shape (allocated once, reused by every call)."""
+    calls of one shape (allocated once, reused by every call).
 
-    def __init__(self, q_host: torch.Tensor, k_host: torch.Tensor, device, chunks: int = 4):
+    The batch is cut into `chunks` pieces.  What is left after the last
+    upload -- that piece's kernel and download -- is the pipeline's tail, so
+    for causal self-attention (q_len == kv_len, no per-sequence lengths) the
+    last batch element is further cut into `tail_pieces` row ranges: rows
+    [r0, r1) see only keys [0, r1), so each piece uploads its own q / k / v
+    rows, computes, and downloads its output rows while the next uploads.
+    A row's result does not depend on the cut (the same key blocks in the
+    same order)."""
+
+    def __init__(self, q_host: torch.Tensor, k_host: torch.Tensor, device, chunks: int = 4, tail_pieces: int = 2):
         if q_host.dim() != 4 or k_host.dim() != 4:
             raise RuntimeError("attention_from_host takes 4-D [batch, seq, heads, head_dim] tensors")
         B = q_host.shape[0]
@@ -31,6 +40,8 @@ class HostAttention:
         self.chunks = max(1, min(chunks, B))
         bounds = [round(i * B / self.chunks) for i in range(self.chunks + 1)]
         self.ranges = [(a, b) for a, b in zip(bounds, bounds[1:]) if b > a]
+        S = q_host.shape[1]
+        self.tail_pieces = max(1, int(tail_pieces)) if S == k_host.shape[1] else 1
         self.qd = torch.empty(q_host.shape, dtype=q_host.dtype, device=self.device)
         self.kd = torch.empty(k_host.shape, dtype=k_host.dtype, device=self.device)
         self.vd = torch.empty(k_host.shape, dtype=k_host.dtype, device=self.device)
@@ -51,11 +62,24 @@ class HostAttention:
         start.record(caller)
         for s in (self.up, self.comp, self.down):
             s.wait_event(start)
-        for a, b in self.ranges:
+        S = q_host.shape[1]
+        row_cut = (self.tail_pieces > 1 and kw.get("causal", True) and kw.get("q_lens") is None
+                   and kw.get("kv_lens") is None and S >= 2 * self.tail_pieces * 128)
+        pieces = []
+        for i, (a, b) in enumerate(self.ranges):
+            if row_cut and i == len(self.ranges) - 1:
+                if b - a > 1:
+                    pieces.append((a, b - 1, 0, S))
+                    a = b - 1
+                rows = [round(p * S / self.tail_pieces / 128) * 128 for p in range(self.tail_pieces)] + [S]
+                pieces += [(a, b, r0, r1) for r0, r1 in zip(rows, rows[1:]) if r1 > r0]
+            else:
+                pieces.append((a, b, 0, S))
+        for a, b, r0, r1 in pieces:
             with torch.cuda.stream(self.up):
-                self.qd[a:b].copy_(q_host[a:b], non_blocking=True)
-                self.kd[a:b].copy_(k_host[a:b], non_blocking=True)
-                self.vd[a:b].copy_(v_host[a:b], non_blocking=True)
+                self.qd[a:b, r0:r1].copy_(q_host[a:b, r0:r1], non_blocking=True)
+                self.kd[a:b, r0:r1].copy_(k_host[a:b, r0:r1], non_blocking=True)
+                self.vd[a:b, r0:r1].copy_(v_host[a:b, r0:r1], non_blocking=True)
                 up_done = torch.cuda.Event()
                 up_done.record(self.up)
             self.comp.wait_event(up_done)
@@ -64,12 +88,14 @@ class HostAttention:
                 for name in ("q_lens", "kv_lens"):
                     if kwc.get(name) is not None:
                         kwc[name] = kwc[name][a:b]  # per-sequence lengths of the chunk
-                ops.single_mha_attention_half(self.od[a:b], self.qd[a:b], self.kd[a:b], self.vd[a:b], sm_scale, **kwc)
+                # a row piece [r0, r1) of causal self-attention sees keys [0, r1)
+                ops.single_mha_attention_half(self.od[a:b, r0:r1], self.qd[a:b, r0:r1], self.kd[a:b, :r1],
+                                              self.vd[a:b, :r1], sm_scale, **kwc)
                 comp_done = torch.cuda.Event()
                 comp_done.record(self.comp)
             self.down.wait_event(comp_done)
             with torch.cuda.stream(self.down):
-                out_host[a:b].copy_(self.od[a:b], non_blocking=True)
+                out_host[a:b, r0:r1].copy_(self.od[a:b, r0:r1], non_blocking=True)
         end = torch.cuda.Event()
         end.record(self.down)
         caller.wait_event(end)
@@ -79,11 +105,11 @@ class HostAttention:
 
 
 def attention_from_host(out_host, q_host, k_host, v_host, sm_scale: float, *, device="cuda", chunks: int = 4,
-                        **kw) -> None:
+                        tail_pieces: int = 2, **kw) -> None:
     """One host-to-host attention call (allocates its device buffers; use
     HostAttention to reuse them across calls).  Blocks until out_host is
     written.  Keyword arguments are those of single_mha_attention_half
     (alibi_slopes, causal, q_lens, kv_lens as device tensors)."""
-    h = HostAttention(q_host, k_host, device, chunks)
+    h = HostAttention(q_host, k_host, device, chunks, tail_pieces)
     h(out_host, q_host, k_host, v_host, sm_scale, **kw)
     torch.cuda.current_stream(h.device).synchronize()
