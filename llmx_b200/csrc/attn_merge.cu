@@ -17,10 +17,10 @@
 // Bandwidth-bound: a block takes one (b, h) and a run of rows_of(D)
 // consecutive rows; the per-row weights go to shared memory once, then every
 // thread moves four 16-byte units of the rows' D elements (units of one row
-// are adjacent lanes), loading all of a partial's units before its
-// arithmetic.  A partial's O is not read where its weight is 0 (rows it does
-// not cover, rows its keys did not reach), so those rows may hold anything.
-// Every byte is read or written once.
+// are adjacent lanes); the first partial's loads are issued before the
+// weights are computed.  A partial's O is read only inside its row range and used
+// only where its weight is non-zero (rows its keys did not reach may hold
+// anything).  Every byte is read or written once.
 #include "common.cuh"
 
 namespace llmx_b200 {
@@ -54,64 +54,96 @@ __host__ __device__ inline int rows_of(int D) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kMergeThreads) lse_merge_kernel(const __grid_constant__ MergeArgs a) {
+__global__ void __launch_bounds__(kMergeThreads, 4) lse_merge_kernel(const __grid_constant__ MergeArgs a) {
   __shared__ float w_s[kMaxParts][kMaxRows];
   __shared__ float inv_s[kMaxRows];
   const int R = rows_of(a.D), V = a.D / 8;
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int s0 = blockIdx.x * R;
+  // Heads are the fastest grid dimension: blocks running together read
+  // whole rows (all heads) of the same row run, contiguous in memory.
+  const int h = blockIdx.x, b = blockIdx.z;
+  const int s0 = blockIdx.y * R;
+  const int rows = min(R, a.S - s0);
+  const int n_units = rows * V;
+  // Partials in groups of kGroup (one: measured fastest on B200, with four
+  // 256-thread blocks per SM; larger groups cost occupancy).  The first
+  // group's O loads are issued before the weights are known (only rows
+  // inside a part's range are read, so every load is in bounds), overlapping
+  // the lse loads below; a loaded value is used only where its weight is
+  // non-zero (rows a part's keys did not reach may hold anything).
+  constexpr int kGroup = 1;
+  uint4 raw[kGroup][kUnitsPerThread];
+  auto load_group = [&](int c0) {
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+      const int c = c0 + g;
+      const bool live = c < a.n_parts && !(s0 + rows <= a.p[c].row_lo || s0 >= a.p[c].row_hi);
+      const T *src = live ? static_cast<const T *>(a.p[c].o) + b * a.p[c].os[0] + h * a.p[c].os[2] : nullptr;
+#pragma unroll
+      for (int k = 0; k < kUnitsPerThread; ++k) {
+        const int idx = threadIdx.x + k * kMergeThreads;
+        raw[g][k] = make_uint4(0u, 0u, 0u, 0u);
+        if (live && idx < n_units) {
+          const int r = idx / V, u = idx - r * V;
+          const int s = s0 + r;
+          if (s >= a.p[c].row_lo && s < a.p[c].row_hi)
+            raw[g][k] = *reinterpret_cast<const uint4 *>(src + (long long)(s - a.p[c].row_lo) * a.p[c].os[1] + u * 8);
+        }
+      }
+    }
+  };
+  load_group(0);
   for (int r = threadIdx.x; r < R; r += kMergeThreads) {
     const int s = s0 + r;
     if (s >= a.S) break;
-    auto part_lse = [&](int c) {
-      const PartDev &p = a.p[c];
-      return (s >= p.row_lo && s < p.row_hi) ? p.lse[b * p.ls[0] + h * p.ls[1] + (s - p.row_lo)] : -CUDART_INF_F;
-    };
+    float l[kMaxParts];
+#pragma unroll
+    for (int c = 0; c < kMaxParts; ++c) {
+      l[c] = -CUDART_INF_F;
+      if (c < a.n_parts) {
+        const PartDev &p = a.p[c];
+        if (s >= p.row_lo && s < p.row_hi) l[c] = p.lse[b * p.ls[0] + h * p.ls[1] + (s - p.row_lo)];
+      }
+    }
     float m = -CUDART_INF_F;
-    for (int c = 0; c < a.n_parts; ++c) m = fmaxf(m, part_lse(c));
+#pragma unroll
+    for (int c = 0; c < kMaxParts; ++c) m = fmaxf(m, l[c]);
     float ws = 0.f;
-    for (int c = 0; c < a.n_parts; ++c) {
-      const float l = part_lse(c);
-      const float w = (l == -CUDART_INF_F) ? 0.f : expf(l - m);
-      w_s[c][r] = w;
-      ws += w;
+#pragma unroll
+    for (int c = 0; c < kMaxParts; ++c) {
+      if (c < a.n_parts) {
+        const float w = (l[c] == -CUDART_INF_F) ? 0.f : expf(l[c] - m);
+        w_s[c][r] = w;
+        ws += w;
+      }
     }
     inv_s[r] = ws > 0.f ? 1.f / ws : 0.f;
     if (a.lse_out != nullptr)
       a.lse_out[((long long)b * a.H + h) * a.S + s] = ws > 0.f ? m + logf(ws) : -CUDART_INF_F;
   }
   __syncthreads();
-  const int rows = min(R, a.S - s0);
-  const int n_units = rows * V;
   float acc[kUnitsPerThread][8];
 #pragma unroll
   for (int k = 0; k < kUnitsPerThread; ++k)
 #pragma unroll
     for (int x = 0; x < 8; ++x) acc[k][x] = 0.f;
-  for (int c = 0; c < a.n_parts; ++c) {
-    const PartDev &p = a.p[c];
-    if (s0 + rows <= p.row_lo || s0 >= p.row_hi) continue;  // the whole run is outside the part
-    const T *src = static_cast<const T *>(p.o) + b * p.os[0] + h * p.os[2];
-    uint4 raw[kUnitsPerThread];
+  for (int c0 = 0; c0 < a.n_parts; c0 += kGroup) {
+    if (c0 > 0) load_group(c0);
 #pragma unroll
-    for (int k = 0; k < kUnitsPerThread; ++k) {
-      const int idx = threadIdx.x + k * kMergeThreads;
-      raw[k] = make_uint4(0u, 0u, 0u, 0u);
-      if (idx < n_units) {
-        const int r = idx / V, u = idx - r * V;
-        if (w_s[c][r] != 0.f)
-          raw[k] = *reinterpret_cast<const uint4 *>(src + (long long)(s0 + r - p.row_lo) * p.os[1] + u * 8);
-      }
-    }
+    for (int g = 0; g < kGroup; ++g) {
+      const int c = c0 + g;
+      if (c >= a.n_parts) break;
 #pragma unroll
-    for (int k = 0; k < kUnitsPerThread; ++k) {
-      const int idx = threadIdx.x + k * kMergeThreads;
-      if (idx < n_units) {
-        const float w = w_s[c][idx / V];
-        float f[8];
-        unpack8<T>(raw[k], f);
+      for (int k = 0; k < kUnitsPerThread; ++k) {
+        const int idx = threadIdx.x + k * kMergeThreads;
+        if (idx < n_units) {
+          const float w = w_s[c][idx / V];
+          if (w != 0.f) {
+            float f[8];
+            unpack8<T>(raw[g][k], f);
 #pragma unroll
-        for (int x = 0; x < 8; ++x) acc[k][x] = fmaf(w, f[x], acc[k][x]);
+            for (int x = 0; x < 8; ++x) acc[k][x] = fmaf(w, f[x], acc[k][x]);
+          }
+        }
       }
     }
   }
@@ -188,7 +220,9 @@ extern "C" llmx_status llmx_attn_lse_merge(int32_t n_parts, const llmx_merge_par
     d.row_hi = p.row_hi;
   }
   const int R = rows_of(head_dim);
-  const dim3 grid((unsigned)((seq + R - 1) / R), (unsigned)n_heads, (unsigned)batch);
+  if ((seq + R - 1) / R > 65535)
+    return record_error(LLMX_ERR_INVALID_ARGUMENT, "lse merge: seq too long for one launch (at most 65535 row runs)");
+  const dim3 grid((unsigned)n_heads, (unsigned)((seq + R - 1) / R), (unsigned)batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == LLMX_FP16)
     lse_merge_kernel<__half><<<grid, kMergeThreads, 0, st>>>(m);

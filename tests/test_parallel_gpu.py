@@ -150,6 +150,39 @@ def test_merge_kernel_matches_oracle(dtype, n_parts, S, H, D):
     torch.testing.assert_close(lse_out.cpu()[fin], lref[fin], atol=1e-4, rtol=0)
 
 
+def test_merge_kernel_full_slice():
+    """One rank's row slice of the 32768-token split at 4 GPUs: four bf16
+    partials of 8192 rows x 32 heads x 128 (one covering only its later
+    rows), merged by the kernel against the same merge in fp32 torch on the
+    GPU (the formula the oracle's merge, pinned above, states)."""
+    B, S, H, D = 1, 8192, 32, 128
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ranges = [(0, S), (0, S), (1000, S), (0, S)]
+    parts = []
+    for lo, hi in ranges:
+        o = torch.randn(B, hi - lo, H, D, generator=g, device="cuda").to(torch.bfloat16)
+        lse = torch.randn(B, H, hi - lo, generator=g, device="cuda") * 4
+        lse[:, :, ::97] = float("-inf")
+        parts.append((o, lse, lo, hi))
+    out = torch.empty(B, S, H, D, dtype=torch.bfloat16, device="cuda")
+    lse_out = torch.empty(B, H, S, device="cuda")
+    parallel.CudaOps().merge(parts, out, lse_out)
+    # fp32 reference: every part padded to all rows with lse = -inf
+    L = torch.full((len(parts), B, H, S), float("-inf"), device="cuda")
+    O = torch.zeros(len(parts), B, S, H, D, device="cuda")
+    for c, (o, lse, lo, hi) in enumerate(parts):
+        L[c, :, :, lo:hi] = lse
+        O[c, :, lo:hi] = o.float()
+    m = L.max(dim=0).values
+    w = torch.where(L == float("-inf"), torch.zeros_like(L), torch.exp(L - m))
+    W = w.sum(dim=0)
+    ref = (w.permute(0, 1, 3, 2).unsqueeze(-1) * O).sum(dim=0) / W.permute(0, 2, 1).unsqueeze(-1).clamp_min(1e-30)
+    torch.cuda.synchronize()
+    assert (out.float() - ref).abs().max().item() <= 2e-2
+    fin = W > 0
+    torch.testing.assert_close(lse_out[fin], (m + torch.log(W))[fin], atol=1e-4, rtol=1e-6)
+
+
 @pytest.mark.parametrize("world", [2, 3, 8])
 def test_unit_and_head_shards_match_the_whole_call(world):
     B, S, H, D = 3, 512, 8, 128
