@@ -239,6 +239,42 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(AttnArgs a, int chu
   const int ql = clamp_len(a.q_lens, b, a.Sq);
   const int kl = ql > 0 ? clamp_len(a.kv_lens, b, a.Skv) : 0;
   const int n_used = max(1, min(n_splits, (kl + chunk - 1) / chunk));
+  if (n_used <= 128) {
+    // Up to 128 splits (one per thread): the split lse values are loaded
+    // once, in parallel, and the weights exp(lse_s - max) go to shared
+    // memory, so each output column is one pass of independent loads.  Same
+    // expressions, in the same split order, as the general path below.
+    __shared__ float w_s[128];
+    __shared__ float red[4];
+    const int tid = threadIdx.x;
+    float l = -CUDART_INF_F;
+    if (kl > 0 && tid < n_used) l = part_lse[((long long)tid * a.B + b) * a.H + h];
+    float m = l;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (tid % 32 == 0) red[tid / 32] = m;
+    __syncthreads();
+    const float mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    if (tid < n_used) w_s[tid] = mx == -CUDART_INF_F ? 0.f : expf(l - mx);
+    __syncthreads();
+    float wsum = 0.f;
+    if (mx != -CUDART_INF_F)
+      for (int sidx = 0; sidx < n_used; ++sidx) wsum += w_s[sidx];
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    T *op = static_cast<T *>(a.o) + b * a.os[0] + h * a.os[2];
+    for (int d = tid; d < D; d += blockDim.x) {
+      float o = 0.f;
+      if (wsum > 0.f) {
+#pragma unroll 4
+        for (int sidx = 0; sidx < n_used; ++sidx)
+          o = fmaf(w_s[sidx], part_o[(((long long)sidx * a.B + b) * a.H + h) * D + d], o);
+      }
+      op[d] = Elem<T>::from_f(o * inv);
+    }
+    if (a.lse != nullptr && tid == 0)
+      a.lse[((long long)b * a.H + h) * a.Sq] = wsum > 0.f ? mx + logf(wsum) : -CUDART_INF_F;
+    return;
+  }
   float mx = -CUDART_INF_F;
   if (kl > 0) {
     for (int sidx = 0; sidx < n_used; ++sidx)
