@@ -464,18 +464,29 @@ def bench_head_split(steps, warmup, rank, world, device, stream, peaks, unsplit)
             "parity": parity}
 
 
-def bench_strong_units(steps, warmup, rank, world, device, stream, peaks):
-    """The Llama-7B-shaped prefill as ONE fixed job (B8 H32 S2048, the same
-    seed on every rank) whose 256 (batch, head) units are dealt over the ranks
-    (parallel.shard_units / run_units), no collective; strong scaling.
-    L2 flushed between steps."""
+def bench_strong_units(steps, warmup, rank, world, device, stream, peaks, name=None):
+    """One fixed job (the same seed on every rank) whose (batch, head) units
+    are dealt over the ranks, no collective; strong scaling.  Units are split
+    by work (parallel.shard_units_weighted): for a prefill each sequence's
+    heads weigh its visible (query, key) pairs, for a decode its key length,
+    so padded batches with unequal lengths still balance.  L2 flushed between
+    steps.  Parity: each rank's units against the whole job on one GPU --
+    bit-identical for a prefill (a unit's result does not depend on the other
+    units); for a decode the split-KV plan depends on how many units a launch
+    holds, so the check is the tolerance of the parity tests."""
     import llmx_b200
     from llmx_b200 import parallel
-    from llmx_b200.workloads import WORKLOADS, flops, make_inputs
+    from llmx_b200.workloads import WORKLOADS, make_inputs, visible_pairs
 
-    w = WORKLOADS[HEADLINE]
+    w = WORKLOADS[name or HEADLINE]
     inp = make_inputs(w, device)  # same seed on every rank: one job
-    start, end = parallel.shard_units(w.batch, w.n_heads, world, rank)
+    if w.is_decode:
+        weights = list(inp.kv_lens_list)
+    else:
+        weights = [visible_pairs(ql, kl, w.causal) for ql, kl in zip(inp.q_lens_list, inp.kv_lens_list)]
+    group = w.n_heads // w.n_kv_heads
+    start, end = parallel.shard_units_weighted(weights, w.n_heads, world, rank, align=group)
+    kw = dict(alibi_slopes=inp.alibi, causal=w.causal, q_lens=inp.q_lens, kv_lens=inp.kv_lens)
     out = torch.zeros_like(inp.q)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     n_launch = [0]
@@ -489,26 +500,32 @@ def bench_strong_units(steps, warmup, rank, world, device, stream, peaks):
             flush.fill_(i & 0xFF)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            n_launch[0] = parallel.run_units(out, inp.q, inp.k, inp.v, start, end, w.sm_scale, causal=w.causal)
+            n_launch[0] = parallel.run_units(out, inp.q, inp.k, inp.v, start, end, w.sm_scale, **kw)
             e1.record(stream)
             if i >= warmup:
                 times.append((e0, e1))
     stream.synchronize()
     per = _max_over_ranks([sum(a.elapsed_time(b) for a, b in times) / steps], world, device)[0]
-    fl = flops(w, inp.q_lens_list, inp.kv_lens_list)
+    work, unit, scale = work_of(w, inp)
     full = torch.empty_like(inp.q)
-    llmx_b200.single_mha_attention_half(full, inp.q, inp.k, inp.v, w.sm_scale, causal=w.causal)
+    llmx_b200.single_mha_attention_half(full, inp.q, inp.k, inp.v, w.sm_scale, **kw)
     torch.cuda.synchronize(device)
-    same = all(torch.equal(out[b0:b1, :, h0:h1], full[b0:b1, :, h0:h1])
-               for b0, b1, h0, h1 in parallel.unit_runs(start, end, w.n_heads))
-    same = _max_over_ranks([0.0 if same else 1.0], world, device)[0] == 0.0
-    return {"kernel": "tcgen05 on this rank's (batch, head) units", "units_per_rank": end - start,
-            "launches_per_step": n_launch[0], "value": fl / (per * 1e-3) / 1e12, "unit": "TFLOP/s",
-            "ms_per_step": per, "scaling": "strong",
-            "roofline": {"bound": "tensor", "achieved": fl / world / (per * 1e-3) / 1e12,
-                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s per GPU",
-                         "frac": fl / world / (per * 1e-3) / 1e12 / peaks["bf16_tflops"]},
-            "parity": {"bitwise_equal_to_single_gpu_call": same, "ok": same}}
+    runs = parallel.unit_runs(start, end, w.n_heads)
+    same = all(torch.equal(out[b0:b1, :, h0:h1], full[b0:b1, :, h0:h1]) for b0, b1, h0, h1 in runs)
+    max_abs = max([(out[b0:b1, :, h0:h1].float() - full[b0:b1, :, h0:h1].float()).abs().max().item()
+                   for b0, b1, h0, h1 in runs] or [0.0])
+    same_all, max_abs_all = _max_over_ranks([0.0 if same else 1.0, max_abs], world, device)
+    ok = same_all == 0.0 if not w.is_decode else max_abs_all <= 2e-2
+    bound = "hbm" if w.is_decode else "tensor"
+    peak = peaks["hbm_gbs"] if w.is_decode else peaks["bf16_tflops"]
+    per_gpu = work / world / (per * 1e-3) / scale
+    return {"kernel": f"{'split-KV decode' if w.is_decode else 'tcgen05'} on this rank's (batch, head) units",
+            "workload": w.name, "units_per_rank": end - start, "launches_per_step": n_launch[0],
+            "value": work / (per * 1e-3) / scale, "unit": unit, "ms_per_step": per, "scaling": "strong",
+            "roofline": {"bound": bound, "achieved": per_gpu, "peak": peak, "unit": f"{unit} per GPU",
+                         "frac": per_gpu / peak},
+            "parity": {"bitwise_equal_to_single_gpu_call": same_all == 0.0, "max_abs_vs_single_gpu_call": max_abs_all,
+                       "ok": ok}}
 
 
 def bench_convert(steps, warmup, rank, world, device, stream, peaks):
@@ -590,6 +607,10 @@ def run_ours(args):
     if not args.no_extra:
         extras[f"llama7b_prefill_strong_{world}gpu"] = bench_strong_units(args.steps, args.warmup, rank, world,
                                                                          device, stream, peaks)
+        extras[f"padded_prefill_strong_{world}gpu"] = bench_strong_units(
+            args.steps, args.warmup, rank, world, device, stream, peaks, "padded_prefill_fp16_b4_h16_s1024_d64")
+        extras[f"bloom_decode_strong_{world}gpu"] = bench_strong_units(
+            args.steps, args.warmup, rank, world, device, stream, peaks, "bloom_decode_bf16_b64_h32_kv4096_d128")
     if world > 1 and not args.no_extra:
         # the single-GPU result every rank checks its share of the long sequence against
         from llmx_b200.workloads import WORKLOADS as _W, make_inputs as _mk

@@ -4,8 +4,9 @@ Three ways the work splits across the GPUs of one node:
 
 * **batch x head shards** (independent units, no communication): every
   (batch, head) pair is an independent attention problem.  ``shard_units``
-  gives each rank a contiguous, balanced slice of the flattened units and
-  ``run_units`` runs the kernel on such a slice (one launch per batch run).
+  gives each rank a contiguous slice of the flattened units of equal count,
+  ``shard_units_weighted`` one of equal work (sequences of unequal length),
+  and ``run_units`` runs the kernel on such a slice (one launch per batch run).
 * **head split** of one long sequence (``head_range``): each rank takes a
   contiguous block of heads, whole GQA groups, and runs the kernel on it; no
   communication.
@@ -63,6 +64,43 @@ def shard_units(batch: int, heads: int, world: int, rank: int) -> Tuple[int, int
     return start, end
 
 
+def shard_units_weighted(weights: Sequence[float], heads: int, world: int, rank: int,
+                         align: int = 1) -> Tuple[int, int]:
+    """Contiguous range [start, end) of flattened (batch, head) units for
+    `rank`, balanced on work instead of unit count: every head of batch
+    element b weighs weights[b] (its key length for decode, its visible
+    (query, key) pairs for prefill).  Boundaries fall on multiples of
+    `align` units (whole GQA groups); each rank's range ends at the first
+    boundary where the running weight reaches (rank + 1) / world of the
+    total, so ranges cover every unit exactly once (some may be empty when
+    there are fewer granules than ranks)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    if align < 1 or heads % align:
+        raise ValueError("align must divide heads")
+    units = len(weights) * heads
+    n_gran = units // align
+    gw = [float(weights[(i * align) // heads]) * align for i in range(n_gran)]
+    total = sum(gw)
+    if total <= 0:
+        g0, g1 = shard_units(1, n_gran, world, rank)
+        return g0 * align, g1 * align
+
+    def edge(r: int) -> int:
+        if r <= 0:
+            return 0
+        if r >= world:
+            return n_gran
+        target, acc = total * r / world, 0.0
+        for i, x in enumerate(gw):
+            if acc + x / 2 >= target:  # the granule goes to the rank holding most of it
+                return i
+            acc += x
+        return n_gran
+
+    return edge(rank) * align, edge(rank + 1) * align
+
+
 def unit_runs(start: int, end: int, heads: int) -> List[Tuple[int, int, int, int]]:
     """The unit range [start, end) as launches: (b0, b1, h0, h1) boxes of whole
     head runs, at most three (a partial first batch, whole batches, a partial
@@ -93,8 +131,12 @@ def run_units(out, q, k, v, start: int, end: int, sm_scale: float, *, alibi_slop
         if h0 % g or h1 % g:
             raise ValueError("a unit shard must hold whole GQA groups")
         a = None if alibi_slopes is None else alibi_slopes[h0:h1]
+        kwr = dict(kw)
+        for name in ("q_lens", "kv_lens"):
+            if kwr.get(name) is not None:
+                kwr[name] = kwr[name][b0:b1]  # per-sequence lengths of the run's batch elements
         ops.single_mha_attention_half(out[b0:b1, :, h0:h1], q[b0:b1, :, h0:h1], k[b0:b1, :, h0 // g:h1 // g],
-                                      v[b0:b1, :, h0 // g:h1 // g], sm_scale, alibi_slopes=a, **kw)
+                                      v[b0:b1, :, h0 // g:h1 // g], sm_scale, alibi_slopes=a, **kwr)
         n += 1
     return n
 

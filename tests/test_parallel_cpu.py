@@ -128,6 +128,38 @@ def test_contiguous_plan_balance_choice():
         parallel.KVSplitPlan.contiguous(S, world, causal=False, balance="pairs").chunks
 
 
+@pytest.mark.parametrize("weights,heads,world,align", [
+    ([565 ** 2, 953 ** 2, 721 ** 2, 968 ** 2], 16, 8, 1),   # padded prefill: visible pairs per sequence
+    ([271, 4010, 1500, 2048, 300, 999], 32, 4, 4),          # decode key lengths, GQA groups of 4
+    ([5, 5, 5, 5], 8, 3, 2),
+    ([1, 0, 7], 2, 8, 1),                                    # more ranks than units: empty ranges
+    ([0, 0], 4, 2, 1),                                       # no work at all: even split
+])
+def test_shard_units_weighted_covers_once_aligned_and_balanced(weights, heads, world, align):
+    ranges = [parallel.shard_units_weighted(weights, heads, world, r, align=align) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == len(weights) * heads
+    for (a0, b0), (a1, b1) in zip(ranges, ranges[1:]):
+        assert a0 <= b0 == a1 <= b1
+    for a, b in ranges:
+        assert a % align == 0 and b % align == 0
+    total = sum(weights) * heads
+    if total > 0:
+        load = [sum(weights[u // heads] for u in range(a, b)) for a, b in ranges]
+        heaviest = max(weights) * align
+        # every rank within one granule of its equal share
+        assert all(abs(x - total / world) <= heaviest for x in load), load
+
+
+def test_shard_units_weighted_equal_weights_match_shard_units():
+    for world in (1, 2, 4, 8):  # an even split: the same ranges
+        assert [parallel.shard_units_weighted([1.0] * 8, 32, world, r) for r in range(world)] == \
+            [parallel.shard_units(8, 32, world, r) for r in range(world)]
+    sizes = [b - a for a, b in (parallel.shard_units_weighted([1.0] * 8, 32, 3, r) for r in range(3))]
+    assert sum(sizes) == 256 and max(sizes) - min(sizes) <= 1  # otherwise sizes within one unit
+    with pytest.raises(ValueError):
+        parallel.shard_units_weighted([1, 2], 6, 2, 0, align=4)
+
+
 @pytest.mark.parametrize("start,end,heads", [(0, 256, 32), (32, 64, 32), (5, 70, 32), (3, 9, 4), (0, 1, 1),
                                              (10, 10, 4)])
 def test_unit_runs_cover_the_range(start, end, heads):

@@ -150,6 +150,53 @@ def test_merge_kernel_matches_oracle(dtype, n_parts, S, H, D):
     torch.testing.assert_close(lse_out.cpu()[fin], lref[fin], atol=1e-4, rtol=0)
 
 
+@pytest.mark.parametrize("world", [3, 8])
+def test_weighted_unit_shards_of_a_padded_batch_match_the_whole_call(world):
+    """Padded, non-causal fp16 prefill with ALiBi (the shape of the padded
+    workload, smaller): units dealt by visible pairs, each shard run with its
+    own sequences' lengths, bit-identical to the whole call."""
+    B, S, H, D = 4, 384, 4, 64
+    lens = [200, 384, 131, 300]
+    q, k, v = (rand(B, S, H, D, seed=20 + s, dtype=torch.float16).cuda() for s in range(3))
+    slopes = oracle.alibi_slopes(H).cuda()
+    ql = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    kw = dict(alibi_slopes=slopes, causal=False, q_lens=ql, kv_lens=ql)
+    full = torch.empty_like(q)
+    llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, **kw)
+    out = torch.full_like(q, float("nan"))
+    weights = [n * n for n in lens]
+    for r in range(world):
+        s0, s1 = parallel.shard_units_weighted(weights, H, world, r)
+        parallel.run_units(out, q, k, v, s0, s1, D ** -0.5, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(out, full)
+
+
+def test_weighted_unit_shards_of_a_decode_batch_match_the_whole_call():
+    """Batched decode with unequal key lengths and GQA: units dealt by key
+    length in whole groups; each shard's split-KV plan may differ from the
+    whole call's, so the check is the parity tolerance (and the oracle)."""
+    B, S, H, Hkv, D = 6, 1024, 8, 2, 128
+    lens = [1024, 37, 500, 777, 1, 256]
+    q = rand(B, 1, H, D, seed=31, dtype=torch.bfloat16).cuda()
+    k, v = (rand(B, S, Hkv, D, seed=32 + s, dtype=torch.bfloat16).cuda() for s in range(2))
+    slopes = oracle.alibi_slopes(H).cuda()
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    kw = dict(alibi_slopes=slopes, kv_lens=kl)
+    full = torch.empty_like(q)
+    llmx_b200.single_mha_attention_half(full, q, k, v, D ** -0.5, **kw)
+    out = torch.full_like(q, float("nan"))
+    for r in range(3):
+        s0, s1 = parallel.shard_units_weighted(lens, H, 3, r, align=H // Hkv)
+        parallel.run_units(out, q, k, v, s0, s1, D ** -0.5, **kw)
+    torch.cuda.synchronize()
+    assert_close(out, full, torch.bfloat16, "decode unit shards vs whole call")
+    for b in (0, 1, 4):
+        ref = oracle.attention_ref(q[b].cpu(), k[b, :lens[b]].cpu(), v[b, :lens[b]].cpu(), sm_scale=D ** -0.5,
+                                   alibi=slopes.cpu())
+        assert_close(out[b], ref, torch.bfloat16, f"decode sequence {b}")
+
+
 def test_merge_kernel_full_slice():
     """One rank's row slice of the 32768-token split at 4 GPUs: four bf16
     partials of 8192 rows x 32 heads x 128 (one covering only its later
