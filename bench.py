@@ -469,7 +469,9 @@ def bench_strong_units(steps, warmup, rank, world, device, stream, peaks, name=N
     are dealt over the ranks, no collective; strong scaling.  Units are split
     by work (parallel.shard_units_weighted): for a prefill each sequence's
     heads weigh its visible (query, key) pairs, for a decode its key length,
-    so padded batches with unequal lengths still balance.  L2 flushed between
+    so padded batches with unequal lengths still balance; in granules of whole
+    sequences or head blocks (parallel.launch_granule), so that a rank runs
+    one launch per run of sequences.  L2 flushed between
     steps.  Parity: each rank's units against the whole job on one GPU --
     bit-identical for a prefill (a unit's result does not depend on the other
     units); for a decode the split-KV plan depends on how many units a launch
@@ -485,7 +487,8 @@ def bench_strong_units(steps, warmup, rank, world, device, stream, peaks, name=N
     else:
         weights = [visible_pairs(ql, kl, w.causal) for ql, kl in zip(inp.q_lens_list, inp.kv_lens_list)]
     group = w.n_heads // w.n_kv_heads
-    start, end = parallel.shard_units_weighted(weights, w.n_heads, world, rank, align=group)
+    granule = parallel.launch_granule(w.batch, w.n_heads, world, group)
+    start, end = parallel.shard_units_weighted(weights, w.n_heads, world, rank, align=granule)
     kw = dict(alibi_slopes=inp.alibi, causal=w.causal, q_lens=inp.q_lens, kv_lens=inp.kv_lens)
     out = torch.zeros_like(inp.q)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
@@ -520,7 +523,8 @@ def bench_strong_units(steps, warmup, rank, world, device, stream, peaks, name=N
     peak = peaks["hbm_gbs"] if w.is_decode else peaks["bf16_tflops"]
     per_gpu = work / world / (per * 1e-3) / scale
     return {"kernel": f"{'split-KV decode' if w.is_decode else 'tcgen05'} on this rank's (batch, head) units",
-            "workload": w.name, "units_per_rank": end - start, "launches_per_step": n_launch[0],
+            "workload": w.name, "units_per_rank": end - start, "unit_granule": granule,
+            "launches_per_step": n_launch[0],
             "value": work / (per * 1e-3) / scale, "unit": unit, "ms_per_step": per, "scaling": "strong",
             "roofline": {"bound": bound, "achieved": per_gpu, "peak": peak, "unit": f"{unit} per GPU",
                          "frac": per_gpu / peak},

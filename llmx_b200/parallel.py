@@ -101,6 +101,25 @@ def shard_units_weighted(weights: Sequence[float], heads: int, world: int, rank:
     return edge(rank) * align, edge(rank + 1) * align
 
 
+def launch_granule(batch: int, heads: int, world: int, group: int = 1) -> int:
+    """The coarsest unit granule for ``shard_units_weighted`` that still
+    gives every rank something to do: whole sequences (`heads` units) when
+    there are at least as many sequences as ranks, else the largest block of
+    whole GQA groups dividing `heads` with batch * heads / granule >= world.
+    Ranges of whole granules cut a rank's units into fewer launches (one per
+    run of whole sequences or one head block), which is what a small job's
+    time depends on: each launch has a fixed cost and fills the GPU only
+    partly."""
+    if world < 1 or heads % group:
+        raise ValueError("world >= 1 and group dividing heads required")
+    g = heads
+    while g > group and (batch * heads) // g < world:
+        g //= 2
+        while g > group and (heads % g or g % group):
+            g -= 1
+    return max(group, g)
+
+
 def unit_runs(start: int, end: int, heads: int) -> List[Tuple[int, int, int, int]]:
     """The unit range [start, end) as launches: (b0, b1, h0, h1) boxes of whole
     head runs, at most three (a partial first batch, whole batches, a partial

@@ -150,6 +150,21 @@ def test_shard_units_weighted_covers_once_aligned_and_balanced(weights, heads, w
         assert all(abs(x - total / world) <= heaviest for x in load), load
 
 
+@pytest.mark.parametrize("batch,heads,world,group,want", [
+    (4, 16, 2, 1, 16), (4, 16, 4, 1, 16), (4, 16, 8, 1, 8), (64, 32, 8, 1, 32), (1, 32, 8, 4, 4),
+    (2, 12, 8, 3, 3), (1, 8, 16, 1, 1), (1, 12, 2, 1, 6)])
+def test_launch_granule(batch, heads, world, group, want):
+    g = parallel.launch_granule(batch, heads, world, group)
+    assert g == want
+    assert heads % g == 0 and g % group == 0
+    # whole-granule ranges give every rank at most one launch per run of sequences
+    w = [1.0 + b for b in range(batch)]
+    for r in range(world):
+        a, b = parallel.shard_units_weighted(w, heads, world, r, align=g)
+        if g == heads:
+            assert len(parallel.unit_runs(a, b, heads)) <= 1
+
+
 def test_shard_units_weighted_equal_weights_match_shard_units():
     for world in (1, 2, 4, 8):  # an even split: the same ranges
         assert [parallel.shard_units_weighted([1.0] * 8, 32, world, r) for r in range(world)] == \
