@@ -1312,17 +1312,25 @@ __device__ bool softmax_256(const AttnArgs &a, Bars256 *bars, uint32_t tmem, int
   const int gi = threadIdx.x & 3;
   const int qi_group = qi - gi;
   T *const obase = static_cast<T *>(a.o) + b * a.os[0] + h * a.os[2];
+  // Two 32-column chunks of O per tensor-memory wait (one wait per 64
+  // columns halves the load latency the 256-column epilogue waits out).
 #pragma unroll 1
-  for (int ch = 0; ch < D / 32; ++ch) {
-    uint32_t o[32];
+  for (int ch2 = 0; ch2 < D / 32; ch2 += 2) {
+    uint32_t o2[2][32];
     if (have) {
-      tmem_ld32(tO + ch * 32, o);
+      tmem_ld32(tO + ch2 * 32, o2[0]);
+      tmem_ld32(tO + (ch2 + 1) * 32, o2[1]);
       tmem_wait_ld();
-      reg_fence32(o);
+      reg_fence32(o2[0]);
+      reg_fence32(o2[1]);
     } else {
 #pragma unroll
-      for (int c = 0; c < 32; ++c) o[c] = 0u;
+      for (int c = 0; c < 32; ++c) o2[0][c] = o2[1][c] = 0u;
     }
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+    const int ch = ch2 + half;
+    uint32_t (&o)[32] = o2[half];
     uint32_t wv[16];
 #pragma unroll
     for (int c = 0; c < 16; ++c)
@@ -1335,6 +1343,7 @@ __device__ bool softmax_256(const AttnArgs &a, Bars256 *bars, uint32_t tmem, int
     for (int k = 0; k < 4; ++k) {
       const int row = qi_group + k;
       if (row < a.Sq) *reinterpret_cast<uint4 *>(obase + (long long)row * a.os[1] + ch * 32 + gi * 8) = u[k];
+    }
     }
   }
   if (a.lse != nullptr && qi < a.Sq)
