@@ -19,6 +19,28 @@ import torch
 from . import ops
 
 
+def plan_pieces(ranges, seq_len: int, tail_pieces: int):
+    """The pipeline's work pieces (b0, b1, r0, r1): batch elements [b0, b1),
+    query rows [r0, r1).  Every chunk of `ranges` is one piece over all rows,
+    except that with tail_pieces > 1 (causal self-attention only) the last
+    batch element is cut into up to `tail_pieces` row ranges with boundaries
+    on multiples of 128 rows (the kernel's query tile), so that a row's result
+    does not depend on the cut; sequences shorter than 2 * tail_pieces * 128
+    rows are not cut.  The pieces cover every (batch, row) once, in order."""
+    tail = tail_pieces if tail_pieces > 1 and seq_len >= 2 * tail_pieces * 128 else 1
+    pieces = []
+    for i, (a, b) in enumerate(ranges):
+        if tail > 1 and i == len(ranges) - 1:
+            if b - a > 1:
+                pieces.append((a, b - 1, 0, seq_len))
+                a = b - 1
+            rows = [round(p * seq_len / tail / 128) * 128 for p in range(tail)] + [seq_len]
+            pieces += [(a, b, r0, r1) for r0, r1 in zip(rows, rows[1:]) if r1 > r0]
+        else:
+            pieces.append((a, b, 0, seq_len))
+    return pieces
+
+
 class HostAttention:
     """Device buffers, streams and events for repeated host-to-host attention
     calls of one shape (allocated once, reused by every call).
@@ -63,18 +85,8 @@ class HostAttention:
         for s in (self.up, self.comp, self.down):
             s.wait_event(start)
         S = q_host.shape[1]
-        row_cut = (self.tail_pieces > 1 and kw.get("causal", True) and kw.get("q_lens") is None
-                   and kw.get("kv_lens") is None and S >= 2 * self.tail_pieces * 128)
-        pieces = []
-        for i, (a, b) in enumerate(self.ranges):
-            if row_cut and i == len(self.ranges) - 1:
-                if b - a > 1:
-                    pieces.append((a, b - 1, 0, S))
-                    a = b - 1
-                rows = [round(p * S / self.tail_pieces / 128) * 128 for p in range(self.tail_pieces)] + [S]
-                pieces += [(a, b, r0, r1) for r0, r1 in zip(rows, rows[1:]) if r1 > r0]
-            else:
-                pieces.append((a, b, 0, S))
+        row_cut = (kw.get("causal", True) and kw.get("q_lens") is None and kw.get("kv_lens") is None)
+        pieces = plan_pieces(self.ranges, S, self.tail_pieces if row_cut else 1)
         for a, b, r0, r1 in pieces:
             with torch.cuda.stream(self.up):
                 self.qd[a:b, r0:r1].copy_(q_host[a:b, r0:r1], non_blocking=True)
