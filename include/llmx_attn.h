@@ -229,7 +229,8 @@ LLMX_API llmx_status llmx_attn_fwd_scatter(const llmx_attn_params *p, const llmx
  * another process opens it with llmx_ipc_open (on its own current device, with
  * peer access enabled as needed) and gets a pointer it can store to;
  * llmx_ipc_close unmaps an opened pointer; llmx_ipc_free frees a buffer this
- * process allocated (after every peer has closed it). */
+ * process allocated (after every peer has closed it).  Both accept NULL and
+ * then do nothing. */
 #define LLMX_IPC_HANDLE_BYTES 64
 LLMX_API llmx_status llmx_ipc_alloc(size_t bytes, void **ptr, void *handle);
 LLMX_API llmx_status llmx_ipc_open(const void *handle, void **ptr);

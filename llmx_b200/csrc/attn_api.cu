@@ -364,12 +364,14 @@ llmx_status llmx_ipc_open(const void *handle, void **ptr) {
 }
 
 llmx_status llmx_ipc_close(void *ptr) {
+  if (ptr == nullptr) return LLMX_OK;  // nothing was opened
   const cudaError_t e = cudaIpcCloseMemHandle(ptr);
   if (e != cudaSuccess) return fail(LLMX_ERR_CUDA, std::string("ipc close: ") + cudaGetErrorString(e));
   return LLMX_OK;
 }
 
 llmx_status llmx_ipc_free(void *ptr) {
+  if (ptr == nullptr) return LLMX_OK;  // as free(NULL)
   const cudaError_t e = cudaFree(ptr);
   if (e != cudaSuccess) return fail(LLMX_ERR_CUDA, std::string("ipc free: ") + cudaGetErrorString(e));
   return LLMX_OK;

@@ -152,3 +152,20 @@ def test_status_strings():
     for code in _lib.STATUS_NAMES:
         assert lib.llmx_status_string(code)
     assert lib.llmx_attn_abi_version() == 3
+
+
+def test_scatter_and_ipc_arguments_checked_before_any_device_work():
+    """The row-scatter and IPC entry points reject bad arguments on the host
+    (no GPU needed), and closing or freeing NULL does nothing."""
+    lib = _lib.load()
+    p = _params()
+    x = _lib.RowScatter()
+    for n_dst, rows, base, msg in [(0, 16, 0, "n_dst"), (9, 16, 0, "n_dst"), (2, 15, 0, "multiples of 16"),
+                                   (2, 16, 3, "multiples of 16")]:
+        x.n_dst, x.slice_rows, x.row_base = n_dst, rows, base
+        assert lib.llmx_attn_fwd_scatter(ctypes.byref(p), ctypes.byref(x), None) == 1  # LLMX_ERR_INVALID_ARGUMENT
+        assert msg in lib.llmx_attn_last_error().decode()
+    assert lib.llmx_ipc_alloc(1024, None, None) == 1  # LLMX_ERR_INVALID_ARGUMENT
+    assert lib.llmx_ipc_open(None, None) == 1  # LLMX_ERR_INVALID_ARGUMENT
+    assert lib.llmx_ipc_close(None) == 0
+    assert lib.llmx_ipc_free(None) == 0
